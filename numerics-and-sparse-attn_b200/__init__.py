@@ -1,0 +1,26 @@
+"""B200 (sm_100a) decode attention: dense GQA, StreamingLLM sink+window and
+KIVI 2-bit, as a drop-in for the reference's dense_kernel.py,
+sparse_kernel.py and quant_kernel.py entry points.
+
+The kernels live in ``libnsa_b200.so`` (C ABI: include/nsa_b200.h), built by
+``build.py``; this package is the thin Python host side over it.
+"""
+from . import _lib
+from .constants import *  # noqa: F401,F403
+from .decode import dense_decode_attention, sparse_decode_attention
+
+__all__ = [
+    "dense_decode_attention",
+    "sparse_decode_attention",
+    "native_library_path",
+    "device_error",
+]
+
+
+def native_library_path() -> str:
+    return _lib.LIB_PATH
+
+
+def device_error(device=None) -> int:
+    """Read and clear the device error word (0 when no kernel timed out)."""
+    return _lib.device_error(device)

@@ -1,0 +1,114 @@
+"""ctypes binding of the C ABI in include/nsa_b200.h.
+
+The shared library is loaded from this package directory only; if it is
+missing the first call raises (there is no CPU fallback).  Status codes from
+the library become Python exceptions: argument problems ValueError, anything
+from the CUDA runtime RuntimeError.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libnsa_b200.so")
+
+NSA_OK = 0
+NSA_ERR_INVALID = 1
+NSA_ERR_ALIGN = 2
+NSA_ERR_UNSUPPORTED = 3
+NSA_ERR_WORKSPACE = 4
+NSA_ERR_CUDA = 5
+NSA_ERR_TIMEOUT = 6
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I32 = ctypes.c_int32
+_F = ctypes.c_float
+_SZ = ctypes.c_size_t
+_INT = ctypes.c_int
+
+# name -> (restype, argtypes); the C declarations are in include/nsa_b200.h
+PROTOTYPES = {
+    "nsa_error_string": (ctypes.c_char_p, [_INT]),
+    "nsa_last_error_message": (ctypes.c_char_p, []),
+    "nsa_device_error": (_INT, [ctypes.POINTER(_INT), _P]),
+    "nsa_version": (ctypes.c_char_p, []),
+    "nsa_dense_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
+    "nsa_dense_decode": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _F, _P, _SZ, _P]),
+    "nsa_sparse_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64]),
+    "nsa_sparse_decode": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _F, _P, _SZ,
+                                 _P]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class NativeError(RuntimeError):
+    """A CUDA-level failure reported by the native library."""
+
+
+def load() -> ctypes.CDLL:
+    """Load libnsa_b200.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"native library {LIB_PATH} is not built; run "
+                    "`python numerics-and-sparse-attn_b200/build.py` (or __graft_entry__.build())")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in PROTOTYPES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def check(status: int) -> None:
+    """Raise the Python exception matching a C status code."""
+    if status == NSA_OK:
+        return
+    lib = load()
+    msg = lib.nsa_last_error_message().decode(errors="replace")
+    name = lib.nsa_error_string(status).decode()
+    if status in (NSA_ERR_INVALID, NSA_ERR_ALIGN, NSA_ERR_UNSUPPORTED):
+        raise ValueError(f"{name}: {msg}")
+    raise NativeError(f"{name}: {msg}")
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def device_error(device: torch.device | None = None) -> int:
+    """Synchronize the current stream and return (and clear) the device error
+    word (NSA_OK when no kernel recorded a timeout)."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    code = _INT(0)
+    with torch.cuda.device(dev):
+        check(load().nsa_device_error(ctypes.byref(code), stream_handle(dev)))
+    return code.value
+
+
+_ws_lock = threading.Lock()
+_workspaces: dict = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Zero-initialised scratch buffer for split-K partials and tickets, one
+    per (device, stream); the kernels leave its counters zeroed again."""
+    key = (device.index, stream_handle(device))
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+    return ws

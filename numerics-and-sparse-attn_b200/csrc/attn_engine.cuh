@@ -1,0 +1,231 @@
+// Warp-level GQA decode-attention engine on mma.sync m16n8k16 (fp16 in, fp32
+// accumulate), shared by the dense, sink+window and KIVI kernels.
+//
+// One warp consumes 16 cached tokens at a time for the 8 query heads of one
+// KV head:
+//   S^T[16 tok x 8 heads]  = K[16 x 128] . Q^T[128 x 8]     (8 k-steps)
+//   online softmax per head (column), exp2 domain
+//   P^T B-operand          = movmatrix.trans of the fp16-packed S^T fragment
+//   O^T[128 x 8] += V^T[128 x 16] . P^T[16 x 8]             (8 m-tiles)
+// The group of 8 query heads is exactly the n = 8 of the instruction, so no
+// lanes are wasted on padding.  K and V tiles are read from shared memory in
+// the layout TMA produces with CU_TENSOR_MAP_SWIZZLE_128B for 64-element
+// (128-byte) boxes: two regions [dims 0-63] and [dims 64-127], each
+// rows x 128 B, 16-byte chunk c of row r stored at chunk c ^ (r % 8).  That
+// makes every ldmatrix phase conflict-free.
+#pragma once
+
+#include "common.cuh"
+
+namespace nsa {
+
+struct WarpAttn {
+  float m[2];       // running max (log2 domain) of heads 2t, 2t+1
+  float l[2];       // per-lane partial softmax denominators of heads 2t, 2t+1
+  float acc[8][4];  // O^T fragments: dims 16j+g / 16j+g+8, heads 2t / 2t+1
+  uint32_t qb[8][2];
+
+  __device__ __forceinline__ void reset() {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      m[i] = -INFINITY;
+      l[i] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[j][c] = 0.f;
+  }
+
+  // Q^T B-fragments from an unswizzled [8 heads][128] fp16 smem block.
+  __device__ __forceinline__ void load_q(uint32_t qbase, int lane) {
+    const int mi = lane >> 3, head = lane & 7;
+#pragma unroll
+    for (int ks = 0; ks < 8; ks += 2) {
+      const int dim = 16 * (ks + (mi >> 1)) + (mi & 1) * 8;
+      ldmatrix_x4(qbase + head * 256 + dim * 2, qb[ks][0], qb[ks][1], qb[ks + 1][0], qb[ks + 1][1]);
+    }
+  }
+
+  // Consume tokens [row0, row0+16) of a swizzled tile whose regions are
+  // `region_bytes` apart.  valid_lo / valid_hi: validity of rows row0+g and
+  // row0+g+8 for this lane (g = lane / 4).
+  __device__ __forceinline__ void consume16(uint32_t kbase, uint32_t vbase, uint32_t region_bytes, int row0,
+                                            bool valid_lo, bool valid_hi, float scale_log2, int lane) {
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      const uint32_t row = row0 + ((lane >> 3) & 1) * 8 + (lane & 7);
+      const uint32_t hi = lane >> 4;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t a0, a1, a2, a3;
+        const uint32_t addr = kbase + (ks >> 2) * region_bytes + swz128(row, 2 * (ks & 3) + hi);
+        ldmatrix_x4(addr, a0, a1, a2, a3);
+        mma_16816(s, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
+      }
+    }
+    // scores in log2 units; masked rows -> -inf
+    s[0] = valid_lo ? s[0] * scale_log2 : -INFINITY;
+    s[1] = valid_lo ? s[1] * scale_log2 : -INFINITY;
+    s[2] = valid_hi ? s[2] * scale_log2 : -INFINITY;
+    s[3] = valid_hi ? s[3] * scale_log2 : -INFINITY;
+    float mx0 = fmaxf(s[0], s[2]);
+    float mx1 = fmaxf(s[1], s[3]);
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float mn0 = fmaxf(m[0], mx0);
+    const float mn1 = fmaxf(m[1], mx1);
+    // reference point: 0 while nothing valid has been seen (avoids inf - inf)
+    const float b0 = (mn0 == -INFINITY) ? 0.f : mn0;
+    const float b1 = (mn1 == -INFINITY) ? 0.f : mn1;
+    const float al0 = fast_exp2(m[0] - b0);
+    const float al1 = fast_exp2(m[1] - b1);
+    const float p0 = fast_exp2(s[0] - b0);
+    const float p1 = fast_exp2(s[1] - b1);
+    const float p2 = fast_exp2(s[2] - b0);
+    const float p3 = fast_exp2(s[3] - b1);
+    l[0] = l[0] * al0 + (p0 + p2);
+    l[1] = l[1] * al1 + (p1 + p3);
+    m[0] = mn0;
+    m[1] = mn1;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      acc[j][0] *= al0;
+      acc[j][1] *= al1;
+      acc[j][2] *= al0;
+      acc[j][3] *= al1;
+    }
+    const uint32_t pb0 = movmatrix_trans(pack_half2(p0, p1));  // P[tok 2t,2t+1][head g]
+    const uint32_t pb1 = movmatrix_trans(pack_half2(p2, p3));  // P[tok 2t+8,2t+9][head g]
+    {
+      const uint32_t mi = lane >> 3;
+      const uint32_t row = row0 + (mi >> 1) * 8 + (lane & 7);
+      const uint32_t hi = mi & 1;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t a0, a1, a2, a3;
+        const uint32_t addr = vbase + (j >> 2) * region_bytes + swz128(row, 2 * (j & 3) + hi);
+        ldmatrix_x4_trans(addr, a0, a1, a2, a3);
+        mma_16816(acc[j], a0, a1, a2, a3, pb0, pb1);
+      }
+    }
+  }
+};
+
+// Cross-warp merge buffers for the epilogue of one (unit, token-range) piece.
+// red_o rows are padded to 132 floats so the fragment scatter is conflict-free.
+constexpr int kRedStride = 132;
+struct EpilogueSmem {
+  float red_o[kConsumerWarps][kGroupHeads][kRedStride];
+  float red_m[kConsumerWarps][kGroupHeads];
+  float red_l[kConsumerWarps][kGroupHeads];
+  int ticket;
+};
+
+// Publish this warp's state to the epilogue buffers.
+__device__ __forceinline__ void warp_publish(const WarpAttn& st, EpilogueSmem& ep, int warp, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  float l0 = st.l[0], l1 = st.l[1];
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    ep.red_o[warp][2 * t][16 * j + g] = st.acc[j][0];
+    ep.red_o[warp][2 * t + 1][16 * j + g] = st.acc[j][1];
+    ep.red_o[warp][2 * t][16 * j + g + 8] = st.acc[j][2];
+    ep.red_o[warp][2 * t + 1][16 * j + g + 8] = st.acc[j][3];
+  }
+  if (g == 0) {
+    ep.red_m[warp][2 * t] = st.m[0];
+    ep.red_m[warp][2 * t + 1] = st.m[1];
+    ep.red_l[warp][2 * t] = l0;
+    ep.red_l[warp][2 * t + 1] = l1;
+  }
+}
+
+// Merge the consumer warps' states for one head and 8 consecutive dims.
+// Returns the normalized output in o[8] and the piece's log2-sum-exp in lse
+// (-inf when the piece saw no valid token; o is then 0/0 = NaN).
+__device__ __forceinline__ void merge_warps(const EpilogueSmem& ep, int head, int d0, float (&o)[8], float& lse) {
+  float mstar = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) mstar = fmaxf(mstar, ep.red_m[w][head]);
+  float f[kConsumerWarps];
+  float L = 0.f;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) {
+    const float mw = ep.red_m[w][head];
+    f[w] = (mw == -INFINITY) ? 0.f : fast_exp2(mw - mstar);
+    L += f[w] * ep.red_l[w][head];
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) a += f[w] * ep.red_o[w][head][d0 + i];
+    o[i] = a / L;
+  }
+  lse = (L > 0.f) ? mstar + log2f(L) : -INFINITY;
+}
+
+__device__ __forceinline__ void store_half8(__half* dst, const float (&o)[8]) {
+  uint4 v;
+  v.x = pack_half2(o[0], o[1]);
+  v.y = pack_half2(o[2], o[3]);
+  v.z = pack_half2(o[4], o[5]);
+  v.w = pack_half2(o[6], o[7]);
+  *reinterpret_cast<uint4*>(dst) = v;
+}
+
+// Split-K partials of one unit: `n` pieces, each [8 heads] lse and
+// [8 heads][128] normalized outputs.  Log-sum-exp combine with warp shuffles:
+// warp `warp` of the consumers reduces heads 2*warp and 2*warp+1; lanes hold
+// pieces for the max / sum, then 4 dims each for the weighted output sum.
+// Reads use ld.global.cg: the partials were written by other SMs.
+__device__ __forceinline__ void combine_pieces(const float* part_lse, const float* part_o, int n, __half* out,
+                                               int warp, int lane) {
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int head = 2 * warp + hh;
+    float M = -INFINITY;
+    for (int i = lane; i < n; i += 32) M = fmaxf(M, __ldcg(part_lse + i * kGroupHeads + head));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float W = 0.f;
+    for (int i = lane; i < n; i += 32) {
+      const float x = __ldcg(part_lse + i * kGroupHeads + head);
+      W += (x == -INFINITY) ? 0.f : fast_exp2(x - M);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) W += __shfl_xor_sync(0xffffffffu, W, off);
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int base = 0; base < n; base += 32) {
+      const int i = base + lane;
+      float x = (i < n) ? __ldcg(part_lse + i * kGroupHeads + head) : -INFINITY;
+      const float wi = (x == -INFINITY) ? 0.f : fast_exp2(x - M);
+      const int cnt = min(32, n - base);
+      for (int j = 0; j < cnt; ++j) {
+        const float wj = __shfl_sync(0xffffffffu, wi, j);
+        if (wj != 0.f) {
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(part_o + ((base + j) * kGroupHeads + head) * kHeadDim) + lane);
+          a.x += wj * v.x;
+          a.y += wj * v.y;
+          a.z += wj * v.z;
+          a.w += wj * v.w;
+        }
+      }
+    }
+    const float inv = 1.f / W;  // W == 0 (no valid token anywhere) -> NaN rows, as the reference's 0/0
+    __half2* dst = reinterpret_cast<__half2*>(out + head * kHeadDim + lane * 4);
+    dst[0] = __floats2half2_rn(a.x * inv, a.y * inv);
+    dst[1] = __floats2half2_rn(a.z * inv, a.w * inv);
+  }
+}
+
+}  // namespace nsa

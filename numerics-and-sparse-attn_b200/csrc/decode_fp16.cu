@@ -1,0 +1,389 @@
+// Dense causal GQA decode and StreamingLLM sink+window decode over float16
+// KV caches (reference: dense_kernel.py:21-82, sparse_kernel.py:15-118).
+//
+// Work decomposition (stream-K split-K): the global space of
+// (unit = batch*kv_head, 64-token tile) is cut into one contiguous, equal
+// slice per persistent CTA (one CTA per SM).  A slice covers pieces of one or
+// more units; a unit split across k CTAs leaves k partial results that the
+// last CTA to finish (atomic ticket, no waiting) merges with a log-sum-exp
+// combine.  Per CTA: warp 4 issues TMA loads of K/V tiles into a 6-stage
+// shared-memory ring (and the 8x128 Q block of each piece into a 2-slot
+// ring); warps 0-3 each consume 16 tokens of every tile on the tensor cores.
+#include "attn_engine.cuh"
+#include "host_util.h"
+
+namespace nsa {
+
+namespace {
+
+constexpr int kStages = 6;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr uint32_t kRegionBytes = kTile * 128;       // one 64-dim half of a tile
+constexpr uint32_t kTileBytes = 2 * kRegionBytes;    // K (or V) tile, 16 KiB
+constexpr uint32_t kStageBytes = 2 * kTileBytes;     // K + V
+constexpr uint32_t kQBytes = kGroupHeads * kHeadDim * 2;
+
+struct Smem {
+  uint8_t kv[kStages][kStageBytes];  // 1024-aligned (swizzle atom)
+  uint8_t q[2][kQBytes];
+  EpilogueSmem ep;
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t q_full[2];
+  uint64_t q_empty[2];
+};
+
+enum Mode : int { kDense = 0, kSparse = 1 };
+
+struct Params {
+  const __half* q;
+  __half* o;
+  int64_t n_units;
+  int n_kv_heads;
+  int mode;
+  int64_t tiles_per_unit;
+  int64_t total_tiles;
+  int n_ctas;
+  int64_t seq_len;
+  const int64_t* seq_lens;
+  const int32_t* ring_heads;
+  int window;
+  int sink;
+  float scale_log2;
+  int max_pieces;
+  int* counters;
+  float* part_lse;
+  float* part_o;
+  int* err;
+};
+
+// CTA owning global tile X under the even split of `total` tiles over `ctas`.
+__device__ __forceinline__ int64_t owner_cta(int64_t X, int64_t total, int64_t ctas) {
+  return ((X + 1) * ctas + total - 1) / total - 1;
+}
+
+__device__ __forceinline__ int64_t unit_len(const Params& p, int64_t unit) {
+  return p.seq_lens ? p.seq_lens[unit / p.n_kv_heads] : p.seq_len;
+}
+
+__device__ __forceinline__ bool slot_valid(const Params& p, int64_t slot, int64_t len, int head) {
+  if (p.mode == kDense) return slot < len;
+  const int64_t S = p.sink, W = p.window;
+  if (slot >= S + W) return false;
+  if (slot < S) return slot < len;
+  int64_t i = (slot - S - head) % W;
+  if (i < 0) i += W;
+  return len - W + i >= S;
+}
+
+// Number of tiles of `unit` that can hold a valid slot (dense: up to len).
+__device__ __forceinline__ int64_t unit_tiles(const Params& p, int64_t unit) {
+  if (p.mode == kDense) {
+    const int64_t len = unit_len(p, unit);
+    return min(p.tiles_per_unit, (len + kTile - 1) / kTile);
+  }
+  return p.tiles_per_unit;
+}
+
+struct Piece {
+  int64_t unit, t_begin, t_end;  // tiles [t_begin, t_end) of unit (after length clipping)
+  int slot, n_pieces;
+};
+
+// Iterates the pieces of this CTA's slice in order.
+struct PieceIter {
+  int64_t X, X1;
+  __device__ PieceIter(const Params& p) {
+    const int64_t c = blockIdx.x;
+    X = c * p.total_tiles / p.n_ctas;
+    X1 = (c + 1) * p.total_tiles / p.n_ctas;
+  }
+  __device__ bool next(const Params& p, Piece& pc) {
+    if (X >= X1) return false;
+    const int64_t tpu = p.tiles_per_unit;
+    pc.unit = X / tpu;
+    const int64_t ub = pc.unit * tpu, ue = ub + tpu;
+    const int64_t e = min(X1, ue);
+    const int64_t nt = unit_tiles(p, pc.unit);
+    pc.t_begin = min(X - ub, nt);
+    pc.t_end = min(e - ub, nt);
+    const int64_t c0 = owner_cta(ub, p.total_tiles, p.n_ctas);
+    const int64_t c1 = owner_cta(ue - 1, p.total_tiles, p.n_ctas);
+    pc.slot = static_cast<int>(blockIdx.x - c0);
+    pc.n_pieces = static_cast<int>(c1 - c0 + 1);
+    X = e;
+    return true;
+  }
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    fp16_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                       const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&sm.full[s]), 1);
+      mbar_init(smem_u32(&sm.empty[s]), kConsumerWarps);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&sm.q_full[s]), 1);
+      mbar_init(smem_u32(&sm.q_empty[s]), kConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      int stage = 0, qs = 0;
+      uint32_t phase = 0, qphase = 0;
+      PieceIter it(p);
+      Piece pc;
+      while (it.next(p, pc)) {
+        // on a timed-out wait the producer stops issuing; consumers then time
+        // out once each and finish without waiting (see below)
+        if (!mbar_wait(smem_u32(&sm.q_empty[qs]), qphase ^ 1, p.err)) return;
+        mbar_arrive_expect_tx(smem_u32(&sm.q_full[qs]), kQBytes);
+        bulk_load(smem_u32(sm.q[qs]), p.q + pc.unit * kGroupHeads * kHeadDim, kQBytes, smem_u32(&sm.q_full[qs]));
+        if (++qs == 2) { qs = 0; qphase ^= 1; }
+        const int u = static_cast<int>(pc.unit);
+        for (int64_t t = pc.t_begin; t < pc.t_end; ++t) {
+          if (!mbar_wait(smem_u32(&sm.empty[stage]), phase ^ 1, p.err)) return;
+          const uint32_t fb = smem_u32(&sm.full[stage]);
+          mbar_arrive_expect_tx(fb, kStageBytes);
+          const uint32_t kd = smem_u32(sm.kv[stage]);
+          const int row = static_cast<int>(t * kTile);
+          tma_load_3d(kd, &tmK, fb, 0, row, u);
+          tma_load_3d(kd + kRegionBytes, &tmK, fb, 64, row, u);
+          tma_load_3d(kd + kTileBytes, &tmV, fb, 0, row, u);
+          tma_load_3d(kd + kTileBytes + kRegionBytes, &tmV, fb, 64, row, u);
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ consumers
+  // A timed-out wait sets `aborted`: the warp then stops waiting (the error
+  // word is already set) but keeps its schedule of named barriers, so the
+  // other consumer warps can never be left waiting on it.
+  int stage = 0, qs = 0;
+  uint32_t phase = 0, qphase = 0;
+  bool aborted = false;
+  const int g = lane >> 2;
+  WarpAttn st;
+  PieceIter it(p);
+  Piece pc;
+  while (it.next(p, pc)) {
+    if (!aborted && !mbar_wait(smem_u32(&sm.q_full[qs]), qphase, p.err)) aborted = true;
+    st.load_q(smem_u32(sm.q[qs]), lane);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&sm.q_empty[qs]));
+    if (++qs == 2) { qs = 0; qphase ^= 1; }
+    st.reset();
+    const int64_t len = unit_len(p, pc.unit);
+    const int head = p.ring_heads ? p.ring_heads[pc.unit / p.n_kv_heads] : 0;
+    for (int64_t t = pc.t_begin; t < pc.t_end; ++t) {
+      const int64_t r0 = t * kTile + 16 * warp;
+      const bool v_lo = slot_valid(p, r0 + g, len, head);
+      const bool v_hi = slot_valid(p, r0 + g + 8, len, head);
+      if (!aborted && !mbar_wait(smem_u32(&sm.full[stage]), phase, p.err)) aborted = true;
+      const uint32_t kd = smem_u32(sm.kv[stage]);
+      st.consume16(kd, kd + kTileBytes, kRegionBytes, 16 * warp, v_lo, v_hi, p.scale_log2, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sm.empty[stage]));
+      if (++stage == kStages) { stage = 0; phase ^= 1; }
+    }
+
+    // ---- epilogue: merge warps, then write the output or a partial
+    warp_publish(st, sm.ep, warp, lane);
+    consumer_sync();
+    const int ct = threadIdx.x;  // 0..127
+    const int hh = ct >> 4, d0 = (ct & 15) * 8;
+    float o[8], lse;
+    merge_warps(sm.ep, hh, d0, o, lse);
+    __half* out = p.o + pc.unit * kGroupHeads * kHeadDim;
+    if (pc.n_pieces == 1) {
+      store_half8(out + hh * kHeadDim + d0, o);
+    } else {
+      const int64_t pidx = pc.unit * p.max_pieces + pc.slot;
+      float* po = p.part_o + (pidx * kGroupHeads + hh) * kHeadDim + d0;
+      reinterpret_cast<float4*>(po)[0] = make_float4(o[0], o[1], o[2], o[3]);
+      reinterpret_cast<float4*>(po)[1] = make_float4(o[4], o[5], o[6], o[7]);
+      if ((ct & 15) == 0) p.part_lse[pidx * kGroupHeads + hh] = lse;
+      __threadfence();
+      consumer_sync();
+      if (ct == 0) sm.ep.ticket = atomicAdd(p.counters + pc.unit, 1);
+      consumer_sync();
+      if (sm.ep.ticket == pc.n_pieces - 1) {
+        __threadfence();
+        const int64_t base = pc.unit * p.max_pieces;
+        combine_pieces(p.part_lse + base * kGroupHeads, p.part_o + base * kGroupHeads * kHeadDim, pc.n_pieces, out,
+                       warp, lane);
+        if (ct == 0) p.counters[pc.unit] = 0;  // ready for the next launch
+      }
+    }
+    consumer_sync();  // epilogue buffers are reused by the next piece
+  }
+}
+
+constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
+
+struct Split {
+  int64_t n_units, tiles_per_unit, total_tiles;
+  int n_ctas, max_pieces;
+};
+
+Split plan(int64_t n_units, int64_t range_slots) {
+  Split s;
+  s.n_units = n_units;
+  s.tiles_per_unit = range_slots > 0 ? (range_slots + kTile - 1) / kTile : 1;
+  s.total_tiles = n_units * s.tiles_per_unit;
+  const int sms = current_device().sm_count > 0 ? current_device().sm_count : 148;
+  s.n_ctas = static_cast<int>(s.total_tiles < sms ? s.total_tiles : sms);
+  if (s.n_ctas < 1) s.n_ctas = 1;
+  // a unit spans at most ceil(tpu * ctas / total) + 1 slices
+  int64_t mp = (s.tiles_per_unit * s.n_ctas + s.total_tiles - 1) / s.total_tiles + 1;
+  if (mp > s.tiles_per_unit) mp = s.tiles_per_unit;
+  s.max_pieces = static_cast<int>(mp);
+  return s;
+}
+
+size_t workspace_bytes(const Split& s) {
+  const size_t counters = ((s.n_units * sizeof(int)) + 255) & ~size_t(255);
+  const size_t pieces = static_cast<size_t>(s.n_units) * s.max_pieces;
+  const size_t lse = ((pieces * kGroupHeads * sizeof(float)) + 255) & ~size_t(255);
+  return counters + lse + pieces * kGroupHeads * kHeadDim * sizeof(float);
+}
+
+int check_common(const void* q, const void* k, const void* v, const void* o, int64_t batch, int64_t n_heads,
+                 int64_t n_kv_heads, int64_t head_dim) {
+  if (!q || !k || !v || !o) return fail(NSA_ERR_INVALID, "null tensor pointer");
+  if (batch < 0 || n_kv_heads <= 0) return fail(NSA_ERR_INVALID, "batch must be >= 0 and n_kv_heads > 0");
+  if (head_dim != kHeadDim) return fail(NSA_ERR_UNSUPPORTED, "head_dim must be 128 (got %lld)", (long long)head_dim);
+  if (n_heads != n_kv_heads * kGroupHeads)
+    return fail(NSA_ERR_UNSUPPORTED, "n_heads must be 8 * n_kv_heads (got %lld, %lld)", (long long)n_heads,
+                (long long)n_kv_heads);
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return fail(NSA_ERR_ALIGN, "q, k, v and o must be 16-byte aligned");
+  if (batch * n_kv_heads > (int64_t(1) << 31) - 1) return fail(NSA_ERR_UNSUPPORTED, "batch * n_kv_heads too large");
+  return NSA_OK;
+}
+
+int launch(Params& p, const Split& s, const void* k, const void* v, int64_t cap, void* ws, size_t ws_bytes,
+           cudaStream_t stream) {
+  if (s.n_units == 0) return NSA_OK;
+  if (cap > (int64_t(1) << 31) - kTile) return fail(NSA_ERR_UNSUPPORTED, "cache length too large for TMA coordinates");
+  const size_t need = workspace_bytes(s);
+  if (!ws || ws_bytes < need)
+    return fail(NSA_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, ws ? ws_bytes : size_t(0));
+  if (!aligned16(ws)) return fail(NSA_ERR_ALIGN, "workspace must be 16-byte aligned");
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  const size_t counters = ((s.n_units * sizeof(int)) + 255) & ~size_t(255);
+  const size_t pieces = static_cast<size_t>(s.n_units) * s.max_pieces;
+  const size_t lse = ((pieces * kGroupHeads * sizeof(float)) + 255) & ~size_t(255);
+  p.counters = reinterpret_cast<int*>(w);
+  p.part_lse = reinterpret_cast<float*>(w + counters);
+  p.part_o = reinterpret_cast<float*>(w + counters + lse);
+  p.n_units = s.n_units;
+  p.tiles_per_unit = s.tiles_per_unit;
+  p.total_tiles = s.total_tiles;
+  p.n_ctas = s.n_ctas;
+  p.max_pieces = s.max_pieces;
+  p.err = device_error_word();
+  if (!p.err) return fail(NSA_ERR_CUDA, "device error word unavailable");
+
+  CUtensorMap mk, mv;
+  const uint64_t dims[3] = {static_cast<uint64_t>(kHeadDim), static_cast<uint64_t>(cap),
+                            static_cast<uint64_t>(s.n_units)};
+  const uint64_t strides[2] = {kHeadDim * 2, static_cast<uint64_t>(cap) * kHeadDim * 2};
+  const uint32_t box[3] = {64, kTile, 1};
+  int rc = encode_tiled(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, k, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_tiled(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+
+  static bool attr_set[64] = {false};
+  const int dev = current_device().device;
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(fp16_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    attr_set[dev] = true;
+  }
+  fp16_decode_kernel<<<s.n_ctas, kThreads, kSmemBytes, stream>>>(mk, mv, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "fp16_decode_kernel launch");
+  return NSA_OK;
+}
+
+}  // namespace
+}  // namespace nsa
+
+using namespace nsa;
+
+extern "C" {
+
+size_t nsa_dense_workspace_bytes(int64_t batch, int64_t n_kv_heads, int64_t seq_len) {
+  if (batch < 0 || n_kv_heads <= 0 || seq_len < 0) return 0;
+  return workspace_bytes(plan(batch * n_kv_heads, seq_len));
+}
+
+int nsa_dense_decode(const void* q, const void* k, const void* v, void* o, int64_t batch, int64_t n_heads,
+                     int64_t n_kv_heads, int64_t head_dim, int64_t cache_len, int64_t seq_len, float sm_scale,
+                     void* workspace, size_t workspace_bytes_, nsa_stream_t stream) {
+  clear_error();
+  int rc = check_common(q, k, v, o, batch, n_heads, n_kv_heads, head_dim);
+  if (rc) return rc;
+  if (seq_len < 0 || cache_len < 1 || seq_len > cache_len)
+    return fail(NSA_ERR_INVALID, "need 0 <= seq_len <= cache_len and cache_len >= 1 (got %lld, %lld)",
+                (long long)seq_len, (long long)cache_len);
+  Params p{};
+  p.q = static_cast<const __half*>(q);
+  p.o = static_cast<__half*>(o);
+  p.n_kv_heads = static_cast<int>(n_kv_heads);
+  p.mode = kDense;
+  p.seq_len = seq_len;
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  const Split s = plan(batch * n_kv_heads, seq_len);
+  return launch(p, s, k, v, cache_len, workspace, workspace_bytes_, stream);
+}
+
+size_t nsa_sparse_workspace_bytes(int64_t batch, int64_t n_kv_heads, int64_t window, int64_t sink) {
+  if (batch < 0 || n_kv_heads <= 0 || window < 0 || sink < 0) return 0;
+  return workspace_bytes(plan(batch * n_kv_heads, window + sink));
+}
+
+int nsa_sparse_decode(const void* q, const void* k_cache, const void* v_cache, void* o, int64_t batch,
+                      int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, int64_t window, int64_t sink,
+                      int64_t seq_len, const int64_t* seq_lens, const int32_t* ring_heads, float sm_scale,
+                      void* workspace, size_t workspace_bytes_, nsa_stream_t stream) {
+  clear_error();
+  int rc = check_common(q, k_cache, v_cache, o, batch, n_heads, n_kv_heads, head_dim);
+  if (rc) return rc;
+  if (window < 0 || sink < 0 || window + sink < 1 || window + sink > (int64_t(1) << 30))
+    return fail(NSA_ERR_INVALID, "need window, sink >= 0 and 1 <= window + sink <= 2^30");
+  if (seq_len < 0) return fail(NSA_ERR_INVALID, "seq_len must be >= 0");
+  Params p{};
+  p.q = static_cast<const __half*>(q);
+  p.o = static_cast<__half*>(o);
+  p.n_kv_heads = static_cast<int>(n_kv_heads);
+  p.mode = kSparse;
+  p.seq_len = seq_len;
+  p.seq_lens = seq_lens;
+  p.ring_heads = ring_heads;
+  p.window = static_cast<int>(window);
+  p.sink = static_cast<int>(sink);
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  const Split s = plan(batch * n_kv_heads, window + sink);
+  return launch(p, s, k_cache, v_cache, window + sink, workspace, workspace_bytes_, stream);
+}
+
+}  // extern "C"

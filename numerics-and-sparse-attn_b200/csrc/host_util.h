@@ -1,0 +1,42 @@
+// Host-side helpers shared by the C-ABI launchers: status/message plumbing,
+// device properties, and TMA tensor-map encoding through the driver entry
+// point (no link-time dependency on libcuda).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdio>
+#include <string>
+
+#include "nsa_b200.h"
+
+namespace nsa {
+
+// Records a formatted message for nsa_last_error_message() and returns code.
+int fail(int code, const char* fmt, ...);
+// Clears the last message (call at entry of every API function).
+void clear_error();
+// Converts a CUDA runtime status into NSA_ERR_CUDA with a message.
+int cuda_fail(cudaError_t e, const char* what);
+
+// Device error word of the current device (a __device__ int, no allocation).
+int* device_error_word();
+
+struct DeviceInfo {
+  int device = -1;
+  int sm_count = 0;
+  int max_smem_optin = 0;
+};
+// Properties of the current device (cached per device).
+const DeviceInfo& current_device();
+
+// cuTensorMapEncodeTiled via cudaGetDriverEntryPoint.
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, const void* base,
+                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                 CUtensorMapSwizzle swizzle);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace nsa

@@ -1,0 +1,113 @@
+"""Host side of the fp16-cache decode paths (dense, sink+window).
+
+Mirrors the reference's Python entry points -- same names, argument meaning
+and defaults -- and forwards to the C ABI (include/nsa_b200.h).  Differences,
+all strict supersets:
+
+* shapes come from the tensors, not from module constants, so any batch size
+  and any number of KV heads (with 8 query heads each) work;
+* ``dense_decode_attention`` accepts ``seq_len <= k.shape[2]`` (a cache with
+  spare capacity) instead of requiring equality;
+* ``sparse_decode_attention`` also reads a ring-buffer cache (``ring_head``)
+  and per-sequence lengths (``seq_lens``).
+
+Inputs must be contiguous float16 CUDA tensors with head_dim 128; anything
+else raises ValueError / TypeError.  There is no CPU fallback.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .constants import D_HEAD, SINK_SIZE
+
+
+def _require(cond: bool, msg: str, exc=ValueError):
+    if not cond:
+        raise exc(msg)
+
+
+def _check_fp16_cuda(name: str, t: torch.Tensor, ndim: int):
+    _require(isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor", TypeError)
+    _require(t.is_cuda, f"{name} must be a CUDA tensor (no CPU fallback)")
+    _require(t.dtype == torch.float16, f"{name} must be float16, got {t.dtype}", TypeError)
+    _require(t.dim() == ndim, f"{name} must have {ndim} dims, got shape {tuple(t.shape)}")
+    _require(t.is_contiguous(), f"{name} must be contiguous")
+
+
+def _check_qkv(q, k, v):
+    _check_fp16_cuda("q", q, 3)
+    _check_fp16_cuda("k", k, 4)
+    _check_fp16_cuda("v", v, 4)
+    b, h, d = q.shape
+    _require(k.shape == v.shape, f"k and v shapes differ: {tuple(k.shape)} vs {tuple(v.shape)}")
+    _require(k.shape[0] == b and k.shape[3] == d, f"q {tuple(q.shape)} and k {tuple(k.shape)} disagree")
+    _require(d == D_HEAD, f"head_dim must be {D_HEAD}, got {d}")
+    _require(k.device == q.device and v.device == q.device, "q, k and v must be on the same device")
+    return b, h, k.shape[1], d
+
+
+def dense_decode_attention(q, k, v, seq_len, sm_scale=None):
+    """Dense causal GQA decode (dense_kernel.py:70-82).
+
+    q: [B, H, 128] fp16.  k/v: [B, H/8, L, 128] fp16, L >= seq_len.
+    Attends cache slots [0, seq_len).  Returns o shaped and typed like q.
+    """
+    b, h, hkv, d = _check_qkv(q, k, v)
+    seq_len = int(seq_len)
+    if sm_scale is None:
+        sm_scale = D_HEAD ** -0.5
+    o = torch.empty_like(q)
+    lib = _lib.load()
+    ws_bytes = lib.nsa_dense_workspace_bytes(b, hkv, seq_len)
+    with torch.cuda.device(q.device):
+        ws = _lib.workspace(q.device, ws_bytes)
+        _lib.check(lib.nsa_dense_decode(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), b, h, hkv, d,
+                                        k.shape[2], seq_len, float(sm_scale), ws.data_ptr(), ws.numel(),
+                                        _lib.stream_handle(q.device)))
+    return o
+
+
+def sparse_decode_attention(q, k_cache, v_cache, seq_len, window, sink=SINK_SIZE, sm_scale=None, *,
+                            ring_head=None, seq_lens=None):
+    """StreamingLLM sink + sliding-window decode (sparse_kernel.py:105-118).
+
+    k_cache/v_cache: [B, H/8, sink+window, 128] fp16.  With ``ring_head``
+    None the cache is the reference's compacted layout (slot sink+i holds
+    position seq_len-window+i); an int or an int32 [B] CUDA tensor selects the
+    ring layout (position p >= sink at slot sink + (p-sink) % window, head =
+    (seq_len-sink) % window).  ``seq_lens`` (int64 [B] CUDA) overrides
+    ``seq_len`` per sequence.
+    """
+    b, h, hkv, d = _check_qkv(q, k_cache, v_cache)
+    window, sink, seq_len = int(window), int(sink), int(seq_len)
+    _require(k_cache.shape[2] == sink + window,
+             f"k_cache must hold sink+window = {sink + window} slots, got {k_cache.shape[2]}")
+    if sm_scale is None:
+        sm_scale = D_HEAD ** -0.5
+    heads_ptr = 0
+    heads = None
+    if ring_head is not None:
+        if isinstance(ring_head, torch.Tensor):
+            heads = ring_head
+        else:
+            heads = torch.full((b,), int(ring_head), dtype=torch.int32, device=q.device)
+        _require(heads.dtype == torch.int32 and heads.is_cuda and heads.numel() == b and heads.is_contiguous(),
+                 "ring_head tensor must be a contiguous int32 CUDA tensor of length B")
+        heads_ptr = heads.data_ptr()
+    lens_ptr = 0
+    if seq_lens is not None:
+        _require(isinstance(seq_lens, torch.Tensor) and seq_lens.dtype == torch.int64 and seq_lens.is_cuda
+                 and seq_lens.numel() == b and seq_lens.is_contiguous(),
+                 "seq_lens must be a contiguous int64 CUDA tensor of length B")
+        lens_ptr = seq_lens.data_ptr()
+    o = torch.empty_like(q)
+    lib = _lib.load()
+    ws_bytes = lib.nsa_sparse_workspace_bytes(b, hkv, window, sink)
+    with torch.cuda.device(q.device):
+        ws = _lib.workspace(q.device, ws_bytes)
+        _lib.check(lib.nsa_sparse_decode(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), o.data_ptr(), b, h,
+                                         hkv, d, window, sink, seq_len, lens_ptr or None, heads_ptr or None,
+                                         float(sm_scale), ws.data_ptr(), ws.numel(),
+                                         _lib.stream_handle(q.device)))
+    return o
