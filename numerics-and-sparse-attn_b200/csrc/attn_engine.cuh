@@ -54,6 +54,8 @@ struct WarpAttn {
                                             bool valid_lo, bool valid_hi, float scale_log2, int lane) {
     float s[4] = {0.f, 0.f, 0.f, 0.f};
     {
+      // two accumulators halve the dependent mma chain of the 8 k-steps
+      float s2[4] = {0.f, 0.f, 0.f, 0.f};
       const uint32_t row = row0 + ((lane >> 3) & 1) * 8 + (lane & 7);
       const uint32_t hi = lane >> 4;
 #pragma unroll
@@ -61,8 +63,13 @@ struct WarpAttn {
         uint32_t a0, a1, a2, a3;
         const uint32_t addr = kbase + (ks >> 2) * region_bytes + swz128(row, 2 * (ks & 3) + hi);
         ldmatrix_x4(addr, a0, a1, a2, a3);
-        mma_16816(s, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
+        if (ks & 1)
+          mma_16816(s2, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
+        else
+          mma_16816(s, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
       }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[c] += s2[c];
     }
     // scores in log2 units; masked rows -> -inf
     s[0] = valid_lo ? s[0] * scale_log2 : -INFINITY;
@@ -116,17 +123,55 @@ struct WarpAttn {
 };
 
 // Cross-warp merge buffers for the epilogue of one (unit, token-range) piece.
-// red_o rows are padded to 132 floats so the fragment scatter is conflict-free.
+// Round 1: each warp of group 1 hands its raw state to the warp of group 0
+// with the same index (identical fragment layout, so the merge is
+// element-wise in registers).  Round 2: the group-0 warps publish their
+// merged states to `red`, which aliases `xfer`.  red.o rows are padded to
+// 132 floats so the fragment scatter is conflict-free.
 constexpr int kRedStride = 132;
+constexpr int kXferWords = 36;  // 32 accumulators + 2 maxima + 2 partial sums
 struct EpilogueSmem {
-  float red_o[kConsumerWarps][kGroupHeads][kRedStride];
-  float red_m[kConsumerWarps][kGroupHeads];
-  float red_l[kConsumerWarps][kGroupHeads];
+  union {
+    float xfer[kGroupWarps][kXferWords][32];
+    struct {
+      float o[kGroupWarps][kGroupHeads][kRedStride];
+      float m[kGroupWarps][kGroupHeads];
+      float l[kGroupWarps][kGroupHeads];
+    } red;
+  };
   int ticket;
 };
 
-// Publish this warp's state to the epilogue buffers.
-__device__ __forceinline__ void warp_publish(const WarpAttn& st, EpilogueSmem& ep, int warp, int lane) {
+__device__ __forceinline__ void warp_xfer_out(const WarpAttn& st, EpilogueSmem& ep, int wq, int lane) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) ep.xfer[wq][4 * j + c][lane] = st.acc[j][c];
+  ep.xfer[wq][32][lane] = st.m[0];
+  ep.xfer[wq][33][lane] = st.m[1];
+  ep.xfer[wq][34][lane] = st.l[0];
+  ep.xfer[wq][35][lane] = st.l[1];
+}
+
+__device__ __forceinline__ void warp_xfer_in(WarpAttn& st, const EpilogueSmem& ep, int wq, int lane) {
+  float fa[2], fb[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const float mb = ep.xfer[wq][32 + h][lane];
+    const float mn = fmaxf(st.m[h], mb);
+    fa[h] = (st.m[h] == -INFINITY) ? 0.f : fast_exp2(st.m[h] - mn);
+    fb[h] = (mb == -INFINITY) ? 0.f : fast_exp2(mb - mn);
+    st.m[h] = mn;
+    st.l[h] = fa[h] * st.l[h] + fb[h] * ep.xfer[wq][34 + h][lane];
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) st.acc[j][c] = fa[c & 1] * st.acc[j][c] + fb[c & 1] * ep.xfer[wq][4 * j + c][lane];
+}
+
+// Publish a group-0 warp's (merged) state to the epilogue buffers.
+__device__ __forceinline__ void warp_publish(const WarpAttn& st, EpilogueSmem& ep, int wq, int lane) {
   const int g = lane >> 2, t = lane & 3;
   float l0 = st.l[0], l1 = st.l[1];
 #pragma unroll
@@ -136,96 +181,97 @@ __device__ __forceinline__ void warp_publish(const WarpAttn& st, EpilogueSmem& e
   }
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    ep.red_o[warp][2 * t][16 * j + g] = st.acc[j][0];
-    ep.red_o[warp][2 * t + 1][16 * j + g] = st.acc[j][1];
-    ep.red_o[warp][2 * t][16 * j + g + 8] = st.acc[j][2];
-    ep.red_o[warp][2 * t + 1][16 * j + g + 8] = st.acc[j][3];
+    ep.red.o[wq][2 * t][16 * j + g] = st.acc[j][0];
+    ep.red.o[wq][2 * t + 1][16 * j + g] = st.acc[j][1];
+    ep.red.o[wq][2 * t][16 * j + g + 8] = st.acc[j][2];
+    ep.red.o[wq][2 * t + 1][16 * j + g + 8] = st.acc[j][3];
   }
   if (g == 0) {
-    ep.red_m[warp][2 * t] = st.m[0];
-    ep.red_m[warp][2 * t + 1] = st.m[1];
-    ep.red_l[warp][2 * t] = l0;
-    ep.red_l[warp][2 * t + 1] = l1;
+    ep.red.m[wq][2 * t] = st.m[0];
+    ep.red.m[wq][2 * t + 1] = st.m[1];
+    ep.red.l[wq][2 * t] = l0;
+    ep.red.l[wq][2 * t + 1] = l1;
   }
 }
 
-// Merge the consumer warps' states for one head and 8 consecutive dims.
-// Returns the normalized output in o[8] and the piece's log2-sum-exp in lse
+// Merge the published group-0 warp states for one head and 4 consecutive dims.
+// Returns the normalized output in o[4] and the piece's log2-sum-exp in lse
 // (-inf when the piece saw no valid token; o is then 0/0 = NaN).
-__device__ __forceinline__ void merge_warps(const EpilogueSmem& ep, int head, int d0, float (&o)[8], float& lse) {
+__device__ __forceinline__ void merge_warps(const EpilogueSmem& ep, int head, int d0, float (&o)[4], float& lse) {
   float mstar = -INFINITY;
 #pragma unroll
-  for (int w = 0; w < kConsumerWarps; ++w) mstar = fmaxf(mstar, ep.red_m[w][head]);
-  float f[kConsumerWarps];
+  for (int w = 0; w < kGroupWarps; ++w) mstar = fmaxf(mstar, ep.red.m[w][head]);
+  float f[kGroupWarps];
   float L = 0.f;
 #pragma unroll
-  for (int w = 0; w < kConsumerWarps; ++w) {
-    const float mw = ep.red_m[w][head];
+  for (int w = 0; w < kGroupWarps; ++w) {
+    const float mw = ep.red.m[w][head];
     f[w] = (mw == -INFINITY) ? 0.f : fast_exp2(mw - mstar);
-    L += f[w] * ep.red_l[w][head];
+    L += f[w] * ep.red.l[w][head];
   }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < 4; ++i) {
     float a = 0.f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) a += f[w] * ep.red_o[w][head][d0 + i];
+    for (int w = 0; w < kGroupWarps; ++w) a += f[w] * ep.red.o[w][head][d0 + i];
     o[i] = a / L;
   }
   lse = (L > 0.f) ? mstar + log2f(L) : -INFINITY;
 }
 
-__device__ __forceinline__ void store_half8(__half* dst, const float (&o)[8]) {
-  uint4 v;
+__device__ __forceinline__ void store_half4(__half* dst, const float (&o)[4]) {
+  uint2 v;
   v.x = pack_half2(o[0], o[1]);
   v.y = pack_half2(o[2], o[3]);
-  v.z = pack_half2(o[4], o[5]);
-  v.w = pack_half2(o[6], o[7]);
-  *reinterpret_cast<uint4*>(dst) = v;
+  *reinterpret_cast<uint2*>(dst) = v;
 }
 
 // Split-K partials of one unit: `n` pieces, each [8 heads] lse and
 // [8 heads][128] normalized outputs.  Log-sum-exp combine with warp shuffles:
-// warp `warp` of the consumers reduces heads 2*warp and 2*warp+1; lanes hold
-// pieces for the max / sum, then 4 dims each for the weighted output sum.
-// Reads use ld.global.cg: the partials were written by other SMs.
-__device__ __forceinline__ void combine_pieces(const float* part_lse, const float* part_o, int n, __half* out,
-                                               int warp, int lane) {
+// consumer warp w reduces head w; lanes hold pieces for the max / sum, then 4
+// dims each for the weighted output sum.  Reads use ld.global.cg (the
+// partials were written by other SMs); every partial read is zeroed again so
+// the workspace is all-zero between launches whatever its next layout.
+__device__ __forceinline__ void combine_pieces(float* part_lse, float* part_o, int n, __half* out, int warp,
+                                               int lane) {
+  static_assert(kConsumerWarps == kGroupHeads, "one consumer warp per head");
+  const int head = warp;
+  float M = -INFINITY;
+  for (int i = lane; i < n; i += 32) M = fmaxf(M, __ldcg(part_lse + i * kGroupHeads + head));
 #pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    const int head = 2 * warp + hh;
-    float M = -INFINITY;
-    for (int i = lane; i < n; i += 32) M = fmaxf(M, __ldcg(part_lse + i * kGroupHeads + head));
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    float W = 0.f;
-    for (int i = lane; i < n; i += 32) {
-      const float x = __ldcg(part_lse + i * kGroupHeads + head);
-      W += (x == -INFINITY) ? 0.f : fast_exp2(x - M);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) W += __shfl_xor_sync(0xffffffffu, W, off);
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int base = 0; base < n; base += 32) {
-      const int i = base + lane;
-      float x = (i < n) ? __ldcg(part_lse + i * kGroupHeads + head) : -INFINITY;
-      const float wi = (x == -INFINITY) ? 0.f : fast_exp2(x - M);
-      const int cnt = min(32, n - base);
-      for (int j = 0; j < cnt; ++j) {
-        const float wj = __shfl_sync(0xffffffffu, wi, j);
-        if (wj != 0.f) {
-          const float4 v = __ldcg(reinterpret_cast<const float4*>(part_o + ((base + j) * kGroupHeads + head) * kHeadDim) + lane);
-          a.x += wj * v.x;
-          a.y += wj * v.y;
-          a.z += wj * v.z;
-          a.w += wj * v.w;
-        }
-      }
-    }
-    const float inv = 1.f / W;  // W == 0 (no valid token anywhere) -> NaN rows, as the reference's 0/0
-    __half2* dst = reinterpret_cast<__half2*>(out + head * kHeadDim + lane * 4);
-    dst[0] = __floats2half2_rn(a.x * inv, a.y * inv);
-    dst[1] = __floats2half2_rn(a.z * inv, a.w * inv);
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  float W = 0.f;
+  for (int i = lane; i < n; i += 32) {
+    const float x = __ldcg(part_lse + i * kGroupHeads + head);
+    W += (x == -INFINITY) ? 0.f : fast_exp2(x - M);
   }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) W += __shfl_xor_sync(0xffffffffu, W, off);
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int base = 0; base < n; base += 32) {
+    const int i = base + lane;
+    const float x = (i < n) ? __ldcg(part_lse + i * kGroupHeads + head) : -INFINITY;
+    const float wi = (x == -INFINITY) ? 0.f : fast_exp2(x - M);
+    const int cnt = min(32, n - base);
+    for (int j = 0; j < cnt; ++j) {
+      const float wj = __shfl_sync(0xffffffffu, wi, j);
+      float4* src = reinterpret_cast<float4*>(part_o + ((base + j) * kGroupHeads + head) * kHeadDim) + lane;
+      if (wj != 0.f) {
+        const float4 v = __ldcg(src);
+        a.x += wj * v.x;
+        a.y += wj * v.y;
+        a.z += wj * v.z;
+        a.w += wj * v.w;
+      }
+      __stcg(src, make_float4(0.f, 0.f, 0.f, 0.f));
+    }
+  }
+  __syncwarp();
+  for (int i = lane; i < n; i += 32) __stcg(part_lse + i * kGroupHeads + head, 0.f);
+  const float inv = 1.f / W;  // W == 0 (no valid token anywhere) -> NaN rows, as the reference's 0/0
+  __half2* dst = reinterpret_cast<__half2*>(out + head * kHeadDim + lane * 4);
+  dst[0] = __floats2half2_rn(a.x * inv, a.y * inv);
+  dst[1] = __floats2half2_rn(a.z * inv, a.w * inv);
 }
 
 }  // namespace nsa

@@ -16,7 +16,9 @@ namespace nsa {
 constexpr int kHeadDim = 128;     // D (reference constants.py:10)
 constexpr int kGroupHeads = 8;    // query heads per KV head (constants.py:9) == mma n
 constexpr int kTile = 64;         // fp16 tokens per pipeline stage
-constexpr int kConsumerWarps = 4; // each owns 16 tokens of a 64-token tile
+constexpr int kGroupWarps = 4;    // a consumer group: each warp owns 16 tokens of a 64-token tile
+constexpr int kGroups = 2;        // groups take alternate tiles (latency hiding)
+constexpr int kConsumerWarps = kGroupWarps * kGroups;
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s: far above any legal wait
 
 // ---------------------------------------------------------------- addresses

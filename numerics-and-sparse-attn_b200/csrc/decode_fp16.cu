@@ -9,6 +9,8 @@
 // combine.  Per CTA: warp 4 issues TMA loads of K/V tiles into a 6-stage
 // shared-memory ring (and the 8x128 Q block of each piece into a 2-slot
 // ring); warps 0-3 each consume 16 tokens of every tile on the tensor cores.
+#include <cstdlib>
+
 #include "attn_engine.cuh"
 #include "host_util.h"
 
@@ -16,16 +18,29 @@ namespace nsa {
 
 namespace {
 
+// Even, so tile k's stage (k % kStages) is always consumed by the same group
+// (k % kGroups): a group then observes every phase of its stages' barriers,
+// which parity waits require.
 constexpr int kStages = 6;
+static_assert(kStages % kGroups == 0, "each stage must belong to one consumer group");
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr uint32_t kRegionBytes = kTile * 128;       // one 64-dim half of a tile
 constexpr uint32_t kTileBytes = 2 * kRegionBytes;    // K (or V) tile, 16 KiB
 constexpr uint32_t kStageBytes = 2 * kTileBytes;     // K + V
 constexpr uint32_t kQBytes = kGroupHeads * kHeadDim * 2;
 
+// Per-piece facts the consumers need, computed once by the producer and
+// published with the piece's Q block.
+struct PieceMeta {
+  int64_t len;  // sequence length (tokens appended so far)
+  int32_t head; // ring head (sparse)
+  int32_t n_inv;  // sparse: window slots with logical index < n_inv are not valid
+};
+
 struct Smem {
   uint8_t kv[kStages][kStageBytes];  // 1024-aligned (swizzle atom)
   uint8_t q[2][kQBytes];
+  PieceMeta meta[2];
   EpilogueSmem ep;
   uint64_t full[kStages];
   uint64_t empty[kStages];
@@ -51,6 +66,7 @@ struct Params {
   int sink;
   float scale_log2;
   int max_pieces;
+  int unit_aligned;  // 1: every CTA takes whole units (no split-K, no combine)
   int* counters;
   float* part_lse;
   float* part_o;
@@ -66,14 +82,28 @@ __device__ __forceinline__ int64_t unit_len(const Params& p, int64_t unit) {
   return p.seq_lens ? p.seq_lens[unit / p.n_kv_heads] : p.seq_len;
 }
 
-__device__ __forceinline__ bool slot_valid(const Params& p, int64_t slot, int64_t len, int head) {
-  if (p.mode == kDense) return slot < len;
-  const int64_t S = p.sink, W = p.window;
-  if (slot >= S + W) return false;
-  if (slot < S) return slot < len;
-  int64_t i = (slot - S - head) % W;
-  if (i < 0) i += W;
-  return len - W + i >= S;
+__device__ __forceinline__ PieceMeta make_meta(const Params& p, int64_t unit) {
+  PieceMeta m;
+  m.len = unit_len(p, unit);
+  m.head = p.ring_heads ? p.ring_heads[unit / p.n_kv_heads] : 0;
+  // window slot with logical index i holds position len - W + i: valid iff >= S
+  const int64_t n_inv = int64_t(p.sink) - (m.len - p.window);
+  m.n_inv = static_cast<int32_t>(n_inv < 0 ? 0 : (n_inv > p.window ? p.window : n_inv));
+  return m;
+}
+
+// Slot validity (sparse_kernel.py:15-46 plus the ring head), division-free:
+// sink slot s valid iff s < len; window slot s has logical index
+// (s - S - head) mod W, computed with one conditional add since both terms
+// lie in [0, W).
+__device__ __forceinline__ bool slot_valid(const Params& p, int64_t slot, const PieceMeta& m) {
+  if (p.mode == kDense) return slot < m.len;
+  const int s = static_cast<int>(slot);
+  if (s < p.sink) return s < m.len;
+  if (s >= p.sink + p.window) return false;
+  int x = s - p.sink - m.head;
+  if (x < 0) x += p.window;
+  return x >= m.n_inv;
 }
 
 // Number of tiles of `unit` that can hold a valid slot (dense: up to len).
@@ -95,8 +125,13 @@ struct PieceIter {
   int64_t X, X1;
   __device__ PieceIter(const Params& p) {
     const int64_t c = blockIdx.x;
-    X = c * p.total_tiles / p.n_ctas;
-    X1 = (c + 1) * p.total_tiles / p.n_ctas;
+    if (p.unit_aligned) {
+      X = (c * p.n_units / p.n_ctas) * p.tiles_per_unit;
+      X1 = ((c + 1) * p.n_units / p.n_ctas) * p.tiles_per_unit;
+    } else {
+      X = c * p.total_tiles / p.n_ctas;
+      X1 = (c + 1) * p.total_tiles / p.n_ctas;
+    }
   }
   __device__ bool next(const Params& p, Piece& pc) {
     if (X >= X1) return false;
@@ -107,10 +142,15 @@ struct PieceIter {
     const int64_t nt = unit_tiles(p, pc.unit);
     pc.t_begin = min(X - ub, nt);
     pc.t_end = min(e - ub, nt);
-    const int64_t c0 = owner_cta(ub, p.total_tiles, p.n_ctas);
-    const int64_t c1 = owner_cta(ue - 1, p.total_tiles, p.n_ctas);
-    pc.slot = static_cast<int>(blockIdx.x - c0);
-    pc.n_pieces = static_cast<int>(c1 - c0 + 1);
+    if (p.unit_aligned) {
+      pc.slot = 0;
+      pc.n_pieces = 1;
+    } else {
+      const int64_t c0 = owner_cta(ub, p.total_tiles, p.n_ctas);
+      const int64_t c1 = owner_cta(ue - 1, p.total_tiles, p.n_ctas);
+      pc.slot = static_cast<int>(blockIdx.x - c0);
+      pc.n_pieces = static_cast<int>(c1 - c0 + 1);
+    }
     X = e;
     return true;
   }
@@ -126,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_u32(&sm.full[s]), 1);
-      mbar_init(smem_u32(&sm.empty[s]), kConsumerWarps);
+      mbar_init(smem_u32(&sm.empty[s]), kGroupWarps);  // released by the group that consumed it
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(smem_u32(&sm.q_full[s]), 1);
@@ -136,24 +176,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
 
+  // CTA-local tile k (over all pieces in order) lives in stage k % kStages,
+  // phase (k / kStages) & 1, and is consumed by group k % kGroups.
   if (warp == kConsumerWarps) {
     // ---------------------------------------------------------- producer
     if (lane == 0) {
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
-      int stage = 0, qs = 0;
-      uint32_t phase = 0, qphase = 0;
+      int qs = 0;
+      uint32_t qphase = 0;
+      uint32_t k = 0;
       PieceIter it(p);
       Piece pc;
       while (it.next(p, pc)) {
         // on a timed-out wait the producer stops issuing; consumers then time
         // out once each and finish without waiting (see below)
         if (!mbar_wait(smem_u32(&sm.q_empty[qs]), qphase ^ 1, p.err)) return;
+        sm.meta[qs] = make_meta(p, pc.unit);  // published by the arrive below (release)
         mbar_arrive_expect_tx(smem_u32(&sm.q_full[qs]), kQBytes);
         bulk_load(smem_u32(sm.q[qs]), p.q + pc.unit * kGroupHeads * kHeadDim, kQBytes, smem_u32(&sm.q_full[qs]));
         if (++qs == 2) { qs = 0; qphase ^= 1; }
         const int u = static_cast<int>(pc.unit);
-        for (int64_t t = pc.t_begin; t < pc.t_end; ++t) {
+        for (int64_t t = pc.t_begin; t < pc.t_end; ++t, ++k) {
+          const uint32_t stage = k % kStages, phase = (k / kStages) & 1;
           if (!mbar_wait(smem_u32(&sm.empty[stage]), phase ^ 1, p.err)) return;
           const uint32_t fb = smem_u32(&sm.full[stage]);
           mbar_arrive_expect_tx(fb, kStageBytes);
@@ -163,7 +208,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(kd + kRegionBytes, &tmK, fb, 64, row, u);
           tma_load_3d(kd + kTileBytes, &tmV, fb, 0, row, u);
           tma_load_3d(kd + kTileBytes + kRegionBytes, &tmV, fb, 64, row, u);
-          if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
       }
     }
@@ -174,8 +218,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // A timed-out wait sets `aborted`: the warp then stops waiting (the error
   // word is already set) but keeps its schedule of named barriers, so the
   // other consumer warps can never be left waiting on it.
-  int stage = 0, qs = 0;
-  uint32_t phase = 0, qphase = 0;
+  const int grp = warp / kGroupWarps, wq = warp % kGroupWarps;
+  int qs = 0;
+  uint32_t qphase = 0;
+  uint32_t k = 0;
   bool aborted = false;
   const int g = lane >> 2;
   WarpAttn st;
@@ -184,40 +230,44 @@ __global__ void __launch_bounds__(kThreads, 1)
   while (it.next(p, pc)) {
     if (!aborted && !mbar_wait(smem_u32(&sm.q_full[qs]), qphase, p.err)) aborted = true;
     st.load_q(smem_u32(sm.q[qs]), lane);
+    const PieceMeta meta = sm.meta[qs];
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(&sm.q_empty[qs]));
     if (++qs == 2) { qs = 0; qphase ^= 1; }
     st.reset();
-    const int64_t len = unit_len(p, pc.unit);
-    const int head = p.ring_heads ? p.ring_heads[pc.unit / p.n_kv_heads] : 0;
-    for (int64_t t = pc.t_begin; t < pc.t_end; ++t) {
-      const int64_t r0 = t * kTile + 16 * warp;
-      const bool v_lo = slot_valid(p, r0 + g, len, head);
-      const bool v_hi = slot_valid(p, r0 + g + 8, len, head);
+    for (int64_t t = pc.t_begin; t < pc.t_end; ++t, ++k) {
+      if ((k % kGroups) != static_cast<uint32_t>(grp)) continue;
+      const uint32_t stage = k % kStages, phase = (k / kStages) & 1;
+      const int64_t r0 = t * kTile + 16 * wq;
+      const bool v_lo = slot_valid(p, r0 + g, meta);
+      const bool v_hi = slot_valid(p, r0 + g + 8, meta);
       if (!aborted && !mbar_wait(smem_u32(&sm.full[stage]), phase, p.err)) aborted = true;
       const uint32_t kd = smem_u32(sm.kv[stage]);
-      st.consume16(kd, kd + kTileBytes, kRegionBytes, 16 * warp, v_lo, v_hi, p.scale_log2, lane);
+      st.consume16(kd, kd + kTileBytes, kRegionBytes, 16 * wq, v_lo, v_hi, p.scale_log2, lane);
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&sm.empty[stage]));
-      if (++stage == kStages) { stage = 0; phase ^= 1; }
     }
 
-    // ---- epilogue: merge warps, then write the output or a partial
-    warp_publish(st, sm.ep, warp, lane);
+    // ---- epilogue: merge the two groups, then the warps, then write the
+    // output or a split-K partial
+    if (grp == 1) warp_xfer_out(st, sm.ep, wq, lane);
     consumer_sync();
-    const int ct = threadIdx.x;  // 0..127
-    const int hh = ct >> 4, d0 = (ct & 15) * 8;
-    float o[8], lse;
+    if (grp == 0) warp_xfer_in(st, sm.ep, wq, lane);
+    consumer_sync();
+    if (grp == 0) warp_publish(st, sm.ep, wq, lane);
+    consumer_sync();
+    const int ct = threadIdx.x;  // 0..255
+    const int hh = ct >> 5, d0 = (ct & 31) * 4;
+    float o[4], lse;
     merge_warps(sm.ep, hh, d0, o, lse);
     __half* out = p.o + pc.unit * kGroupHeads * kHeadDim;
     if (pc.n_pieces == 1) {
-      store_half8(out + hh * kHeadDim + d0, o);
+      store_half4(out + hh * kHeadDim + d0, o);
     } else {
       const int64_t pidx = pc.unit * p.max_pieces + pc.slot;
       float* po = p.part_o + (pidx * kGroupHeads + hh) * kHeadDim + d0;
-      reinterpret_cast<float4*>(po)[0] = make_float4(o[0], o[1], o[2], o[3]);
-      reinterpret_cast<float4*>(po)[1] = make_float4(o[4], o[5], o[6], o[7]);
-      if ((ct & 15) == 0) p.part_lse[pidx * kGroupHeads + hh] = lse;
+      *reinterpret_cast<float4*>(po) = make_float4(o[0], o[1], o[2], o[3]);
+      if ((ct & 31) == 0) p.part_lse[pidx * kGroupHeads + hh] = lse;
       __threadfence();
       consumer_sync();
       if (ct == 0) sm.ep.ticket = atomicAdd(p.counters + pc.unit, 1);
@@ -238,8 +288,14 @@ constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 
 struct Split {
   int64_t n_units, tiles_per_unit, total_tiles;
-  int n_ctas, max_pieces;
+  int n_ctas, max_pieces, unit_aligned;
 };
+
+// Units of at most this many tiles (1 MiB of K+V) are not split when there
+// are at least as many units as CTAs: a short launch is dominated by fixed
+// per-piece costs (fence, ticket, cross-SM combine), and one SM can stream
+// two such units at well above its fair share of HBM bandwidth.
+constexpr int64_t kWholeUnitMaxTiles = 32;
 
 Split plan(int64_t n_units, int64_t range_slots) {
   Split s;
@@ -249,6 +305,19 @@ Split plan(int64_t n_units, int64_t range_slots) {
   const int sms = current_device().sm_count > 0 ? current_device().sm_count : 148;
   s.n_ctas = static_cast<int>(s.total_tiles < sms ? s.total_tiles : sms);
   if (s.n_ctas < 1) s.n_ctas = 1;
+  const char* env = getenv("NSA_SPLIT_MODE");  // "stream" / "unit": tuning override
+  // Whole units also when the imbalance is mild: the busiest CTA then holds
+  // at most 25% more than the mean, which the idle SMs' bandwidth absorbs.
+  const int64_t per_cta = (n_units + sms - 1) / sms;
+  bool whole = n_units >= sms && (s.tiles_per_unit <= kWholeUnitMaxTiles || per_cta * sms * 4 <= n_units * 5);
+  if (env && env[0] == 's') whole = false;
+  if (env && env[0] == 'u' && n_units >= sms) whole = true;
+  s.unit_aligned = whole ? 1 : 0;
+  if (whole) {
+    s.n_ctas = sms;
+    s.max_pieces = 1;
+    return s;
+  }
   // a unit spans at most ceil(tpu * ctas / total) + 1 slices
   int64_t mp = (s.tiles_per_unit * s.n_ctas + s.total_tiles - 1) / s.total_tiles + 1;
   if (mp > s.tiles_per_unit) mp = s.tiles_per_unit;
@@ -297,6 +366,7 @@ int launch(Params& p, const Split& s, const void* k, const void* v, int64_t cap,
   p.total_tiles = s.total_tiles;
   p.n_ctas = s.n_ctas;
   p.max_pieces = s.max_pieces;
+  p.unit_aligned = s.unit_aligned;
   p.err = device_error_word();
   if (!p.err) return fail(NSA_ERR_CUDA, "device error word unavailable");
 

@@ -104,7 +104,7 @@ def test_sparse_reference_cases_full_batch(L, W):
     q = torch.randn(B, 64, 128, device=DEV, generator=g).half()
     S = 4
     # attended positions: the sink and the last W tokens (no double counting)
-    pos = torch.cat([torch.arange(min(S, L)), torch.arange(max(S, L - W), L)]).tolist()
+    pos = list(range(min(S, L))) + list(range(max(S, L - W), L))
     kv_pos = torch.randn(B, 8, len(pos), 128, device=DEV, generator=g).half()
     vv_pos = torch.randn(B, 8, len(pos), 128, device=DEV, generator=g).half()
     # compacted and ring caches; every slot not holding an attended position
@@ -160,3 +160,27 @@ def test_no_device_error_recorded():
     import importlib
     pkg = importlib.import_module("numerics-and-sparse-attn_b200")
     assert pkg.device_error() == 0
+
+
+@pytest.mark.parametrize("mode", ["stream", "unit", "auto"])
+def test_split_modes_and_workspace_reuse(mode, monkeypatch):
+    """Stream-K (split units, in-launch combine) and unit-aligned schedules
+    give the same answer, and one workspace serves calls of changing shape
+    back to back (the combine leaves it zeroed for any later layout)."""
+    monkeypatch.setenv("NSA_SPLIT_MODE", mode)
+    for kind, B, W, L in [("dense", 2, 0, 1000), ("dense", 32, 0, 4096), ("sparse", 2, 4096, 4100),
+                          ("dense", 32, 0, 2049), ("sparse", 32, 2044, 4000), ("sparse", 32, 4096, 4100),
+                          ("dense", 32, 0, 4100), ("sparse", 8, 256, 5000)]:
+        g = torch.Generator(device=DEV).manual_seed(B * 1000 + L)
+        q = torch.randn(B, 64, 128, device=DEV, generator=g).half()
+        if kind == "dense":
+            k = torch.randn(B, 8, L, 128, device=DEV, generator=g).half()
+            v = torch.randn(B, 8, L, 128, device=DEV, generator=g).half()
+            o = dense_kernel.dense_decode_attention(q, k, v, seq_len=L)
+            ref = oa.dense_attention(q.float(), k.float(), v.float())
+        else:
+            k = torch.randn(B, 8, 4 + W, 128, device=DEV, generator=g).half()
+            v = torch.randn(B, 8, 4 + W, 128, device=DEV, generator=g).half()
+            o = sparse_kernel.sparse_decode_attention(q, k, v, seq_len=L, window=W)
+            ref = oa.sparse_attention_slots(q.float(), k.float(), v.float(), L, W, 4)
+        assert _err(o, ref) < TOL, (mode, kind, B, W, L)
