@@ -153,7 +153,7 @@ class Workload:
             self.ring_head = torch.full((batch,), (self.seq_len - S) % self.window, dtype=torch.int32,
                                         device=device)
         self.out = [None] * self.n_layers
-        self.launches_per_step = 1
+        self.launches_per_step = 2 if name == "kivi" else 1  # kivi: append kernel + attention kernel
 
     def step(self, i: int, q=None, new_k=None, new_v=None):
         j = i % self.n_layers

@@ -90,6 +90,95 @@ int nsa_sparse_decode(const void* q, const void* k_cache, const void* v_cache, v
                       const int64_t* seq_lens, const int32_t* ring_heads, float sm_scale,
                       void* workspace, size_t workspace_bytes, nsa_stream_t stream);
 
+
+/* ------------------------------------------------------------------ KIVI
+ * 2-bit KIVI quantization: K per channel over groups of 32 tokens, V per
+ * token over groups of 32 channels, asymmetric, fp16 scale and zero point,
+ * 4 codes per byte.  dtype of the input: 0 = float32, 1 = float16.
+ *
+ * Replaces quant_kernel.py:106-126 quantize_k_cache(k, group_size, bits) and
+ * its kernel quant_kernel.py:44-103: k [B, Hkv, T, D] (T % 32 == 0) ->
+ * packed u8 [B, Hkv, T/4, D], scale and zero f16 [B, Hkv, T/32, D].
+ * Bit-exact with the reference (IEEE float32 division, round-half-up via
+ * floor(x + 0.5), fp16 round-to-nearest-even stores). */
+int nsa_kivi_quantize_k(const void* k, int dtype, void* packed, void* scale, void* zero,
+                        int64_t batch, int64_t n_kv_heads, int64_t seq_len, int64_t head_dim,
+                        int64_t group_size, int64_t bits, nsa_stream_t stream);
+/* Replaces quant_kernel.py:193-214 quantize_v_cache(v, group_size, bits) and
+ * its kernel quant_kernel.py:129-190: v [B, Hkv, T, D] (D % 32 == 0) ->
+ * packed u8 [B, Hkv, T, D/4], scale and zero f16 [B, Hkv, T, D/32]. */
+int nsa_kivi_quantize_v(const void* v, int dtype, void* packed, void* scale, void* zero,
+                        int64_t batch, int64_t n_kv_heads, int64_t seq_len, int64_t head_dim,
+                        int64_t group_size, int64_t bits, nsa_stream_t stream);
+/* Host-callable dequantization of tokens [tok_start, tok_start + n_tokens)
+ * (positions clamped into [0, seq_len)) to float32 [B, Hkv, n_tokens, D]:
+ * s * (code - z) with the fp16-stored s and z.  Replaces the Triton-only
+ * helpers quant_kernel.py:219-266 _dequantize_k_tile and :269-311
+ * _dequantize_v_tile that test_dequantize_tile_isolated.py:28-63 wraps. */
+int nsa_kivi_dequant_k(const void* packed, const void* scale, const void* zero, void* out,
+                       int64_t batch, int64_t n_kv_heads, int64_t seq_len, int64_t head_dim,
+                       int64_t tok_start, int64_t n_tokens, nsa_stream_t stream);
+int nsa_kivi_dequant_v(const void* packed, const void* scale, const void* zero, void* out,
+                       int64_t batch, int64_t n_kv_heads, int64_t seq_len, int64_t head_dim,
+                       int64_t tok_start, int64_t n_tokens, nsa_stream_t stream);
+
+/* KIVI sink + window decode over the reference's 14-tensor layout, as built
+ * by build_quantized_kv_cache (quant_kernel.py:584-622):
+ *   k_res, v_res      f16 [B, Hkv, R, D]          the R newest window tokens
+ *   k_sink_*          u8 [B, Hkv, 8, D] + f16 [B, Hkv, 1, D] x2   sink padded
+ *   v_sink_*          u8 [B, Hkv, 32, D/4] + f16 [B, Hkv, 32, D/32] x2
+ *   k_win_*           u8 [B, Hkv, (W-R)/4, D] + f16 [B, Hkv, (W-R)/32, D] x2
+ *   v_win_*           u8 [B, Hkv, W-R, D/4] + f16 [B, Hkv, W-R, D/32] x2
+ * Slot validity follows _kv_indices (sparse_kernel.py:15-46) over the
+ * compacted order sink | window-old | residual.  Replaces
+ * quant_kernel.py:551-581 sparse_decode_attention_quantized and its kernel
+ * quant_kernel.py:436-548.  Requires window >= residual,
+ * (window - residual) % 32 == 0, sink <= 32, group_size 32, bits 2. */
+size_t nsa_kivi_workspace_bytes(int64_t batch, int64_t n_kv_heads, int64_t window, int64_t residual);
+int nsa_kivi_decode(const void* q, const void* k_res, const void* v_res,
+                    const void* k_sink_packed, const void* k_sink_scale, const void* k_sink_zero,
+                    const void* v_sink_packed, const void* v_sink_scale, const void* v_sink_zero,
+                    const void* k_win_packed, const void* k_win_scale, const void* k_win_zero,
+                    const void* v_win_packed, const void* v_win_scale, const void* v_win_zero,
+                    void* o, int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+                    int64_t seq_len, int64_t window, int64_t sink, int64_t residual,
+                    int64_t group_size, int64_t bits, float sm_scale,
+                    void* workspace, size_t workspace_bytes, nsa_stream_t stream);
+
+/* Streaming KIVI cache (no reference counterpart: the reference quantizes
+ * once at setup, quant_kernel.py:7-8).  Token p < sink is a sink token; token
+ * p >= sink has stream index i = p - sink.  Unflushed stream tokens live in
+ * an fp16 residual ring of R + 32 slots (slot i % (R+32)); when R + 32 are
+ * unflushed, the oldest 32 are quantized (quantize_k / quantize_v math) into
+ * window group slot g % NG of a ring of NG = (W - R) / 32 groups (dropped
+ * when NG == 0).  Attention covers exactly StreamingLLM's set: the first
+ * min(len, sink) tokens and stream tokens with p >= len - W.  When
+ * (len - sink - R) % 32 == 0 and len >= sink + W the state equals
+ * build_quantized_kv_cache of the same window.  All pointers are device
+ * memory; unit_lens holds the token count of every (batch, kv_head) unit. */
+typedef struct {
+  int64_t batch, n_kv_heads, head_dim;  /* head_dim must be 128 */
+  int64_t window, sink, residual;       /* W; S in [1, 32]; R a positive multiple of 32 */
+  int64_t n_groups;                     /* (W - R) / 32 if W >= R, else 0 */
+  int64_t* unit_lens;                   /* [B * Hkv] tokens appended so far */
+  void* sink_k;                         /* f16 [B, Hkv, S, D] unquantized sink tokens */
+  void* sink_v;
+  void* k_sink_packed, *k_sink_scale, *k_sink_zero;  /* u8 [B,Hkv,8,D]; f16 [B,Hkv,1,D] */
+  void* v_sink_packed, *v_sink_scale, *v_sink_zero;  /* u8 [B,Hkv,32,D/4]; f16 [B,Hkv,32,D/32] */
+  void* k_win_packed, *k_win_scale, *k_win_zero;     /* u8 [B,Hkv,NG*8,D]; f16 [B,Hkv,NG,D] */
+  void* v_win_packed, *v_win_scale, *v_win_zero;     /* u8 [B,Hkv,NG*32,D/4]; f16 [B,Hkv,NG*32,D/32] */
+  void* k_res, *v_res;                               /* f16 [B, Hkv, R + 32, D] */
+} nsa_kivi_stream_cache;
+
+/* Append one token per (batch, kv_head): new_k, new_v f16 [B, Hkv, D];
+ * quantizes a group when one completes and advances unit_lens. */
+int nsa_kivi_append(const nsa_kivi_stream_cache* cache, const void* new_k, const void* new_v,
+                    nsa_stream_t stream);
+/* Decode q [B, 8*Hkv, D] against the streaming cache -> o. */
+size_t nsa_kivi_stream_workspace_bytes(const nsa_kivi_stream_cache* cache);
+int nsa_kivi_stream_decode(const nsa_kivi_stream_cache* cache, const void* q, void* o, float sm_scale,
+                           void* workspace, size_t workspace_bytes, nsa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

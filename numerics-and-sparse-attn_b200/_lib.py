@@ -42,6 +42,15 @@ PROTOTYPES = {
     "nsa_sparse_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64]),
     "nsa_sparse_decode": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _F, _P, _SZ,
                                  _P]),
+    "nsa_kivi_quantize_k": (_INT, [_P, _INT, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
+    "nsa_kivi_quantize_v": (_INT, [_P, _INT, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
+    "nsa_kivi_dequant_k": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
+    "nsa_kivi_dequant_v": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
+    "nsa_kivi_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64]),
+    "nsa_kivi_decode": (_INT, [_P] * 16 + [_I64] * 10 + [_F, _P, _SZ, _P]),
+    "nsa_kivi_append": (_INT, [_P, _P, _P, _P]),
+    "nsa_kivi_stream_workspace_bytes": (_SZ, [_P]),
+    "nsa_kivi_stream_decode": (_INT, [_P, _P, _P, _F, _P, _SZ, _P]),
 }
 
 _lock = threading.Lock()

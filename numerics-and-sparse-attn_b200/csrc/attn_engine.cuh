@@ -214,9 +214,9 @@ __device__ __forceinline__ void merge_warps(const EpilogueSmem& ep, int head, in
     float a = 0.f;
 #pragma unroll
     for (int w = 0; w < kGroupWarps; ++w) a += f[w] * ep.red.o[w][head][d0 + i];
-    o[i] = a / L;
+    o[i] = __fdividef(a, L);  // L == 0 (nothing attended): 0/0 = NaN, as the reference
   }
-  lse = (L > 0.f) ? mstar + log2f(L) : -INFINITY;
+  lse = (L > 0.f) ? mstar + __log2f(L) : -INFINITY;
 }
 
 __device__ __forceinline__ void store_half4(__half* dst, const float (&o)[4]) {
@@ -268,7 +268,7 @@ __device__ __forceinline__ void combine_pieces(float* part_lse, float* part_o, i
   }
   __syncwarp();
   for (int i = lane; i < n; i += 32) __stcg(part_lse + i * kGroupHeads + head, 0.f);
-  const float inv = 1.f / W;  // W == 0 (no valid token anywhere) -> NaN rows, as the reference's 0/0
+  const float inv = __fdividef(1.f, W);  // W == 0 (no valid token anywhere) -> inf * 0 = NaN, as the reference's 0/0
   __half2* dst = reinterpret_cast<__half2*>(out + head * kHeadDim + lane * 4);
   dst[0] = __floats2half2_rn(a.x * inv, a.y * inv);
   dst[1] = __floats2half2_rn(a.z * inv, a.w * inv);

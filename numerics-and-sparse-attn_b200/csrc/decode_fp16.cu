@@ -123,7 +123,7 @@ struct Piece {
 // Iterates the pieces of this CTA's slice in order.
 struct PieceIter {
   int64_t X, X1;
-  __device__ PieceIter(const Params& p) {
+  __device__ __forceinline__ PieceIter(const Params& p) {
     const int64_t c = blockIdx.x;
     if (p.unit_aligned) {
       X = (c * p.n_units / p.n_ctas) * p.tiles_per_unit;
@@ -133,7 +133,7 @@ struct PieceIter {
       X1 = (c + 1) * p.total_tiles / p.n_ctas;
     }
   }
-  __device__ bool next(const Params& p, Piece& pc) {
+  __device__ __forceinline__ bool next(const Params& p, Piece& pc) {
     if (X >= X1) return false;
     const int64_t tpu = p.tiles_per_unit;
     pc.unit = X / tpu;

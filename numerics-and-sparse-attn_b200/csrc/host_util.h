@@ -40,3 +40,8 @@ int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, con
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace nsa
+
+namespace nsa {
+// Validates an nsa_kivi_stream_cache descriptor (shared by append / decode).
+int kivi_check_stream_cache(const nsa_kivi_stream_cache& c);
+}  // namespace nsa

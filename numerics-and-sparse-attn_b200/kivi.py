@@ -1,0 +1,380 @@
+"""Host side of the KIVI 2-bit paths.
+
+Reference-shaped entry points (same names, arguments and return values as
+quant_kernel.py): ``quantize_k_cache``, ``quantize_v_cache``,
+``build_quantized_kv_cache``, ``sparse_decode_attention_quantized``, plus
+host-callable ``dequantize_k`` / ``dequantize_v`` (the reference's
+``_dequantize_k_tile`` / ``_dequantize_v_tile`` are Triton-only helpers).
+
+``KiviCache`` is the streaming cache the reference lacks: one new token per
+sequence per step is appended and quantized on the GPU (quantize-on-append),
+then attention reads sink + quantized window + fp16 residual.  Its layout and
+semantics are documented with ``nsa_kivi_stream_cache`` in include/nsa_b200.h.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .constants import D_HEAD, GROUP_SIZE, QUANT_BITS, RESIDUAL_SIZE, SINK_SIZE
+
+
+def _req(cond, msg, exc=ValueError):
+    if not cond:
+        raise exc(msg)
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return 0
+    if t.dtype == torch.float16:
+        return 1
+    raise TypeError(f"quantizer input must be float32 or float16, got {t.dtype}")
+
+
+def _check_cuda4(name, t):
+    _req(isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor", TypeError)
+    _req(t.is_cuda, f"{name} must be a CUDA tensor (no CPU fallback)")
+    _req(t.dim() == 4, f"{name} must be [batch, kv_heads, seq, head_dim], got {tuple(t.shape)}")
+
+
+def quantize_k_cache(k, group_size=GROUP_SIZE, bits=QUANT_BITS):
+    """quant_kernel.py:106-126.  k: [B, Hkv, T, D] float32 (or float16),
+    T % group_size == 0.  Returns (packed u8 [B,Hkv,T/4,D], scale f16
+    [B,Hkv,T/G,D], zero_point f16 [B,Hkv,T/G,D]), bit-exact with the reference."""
+    _check_cuda4("k", k)
+    b, h, t, d = k.shape
+    # the reference asserts this (quant_kernel.py:110)
+    assert t % group_size == 0, "this simple version assumes seq_len is a multiple of group_size"
+    k = k.contiguous()
+    packed = torch.empty((b, h, t // 4, d), dtype=torch.uint8, device=k.device)
+    scale = torch.empty((b, h, t // group_size, d), dtype=torch.float16, device=k.device)
+    zero = torch.empty_like(scale)
+    with torch.cuda.device(k.device):
+        _lib.check(_lib.load().nsa_kivi_quantize_k(k.data_ptr(), _dtype_code(k), packed.data_ptr(), scale.data_ptr(),
+                                                   zero.data_ptr(), b, h, t, d, group_size, bits,
+                                                   _lib.stream_handle(k.device)))
+    return packed, scale, zero
+
+
+def quantize_v_cache(v, group_size=GROUP_SIZE, bits=QUANT_BITS):
+    """quant_kernel.py:193-214.  v: [B, Hkv, T, D] float32 (or float16),
+    D % group_size == 0.  Returns (packed u8 [B,Hkv,T,D/4], scale f16
+    [B,Hkv,T,D/G], zero_point f16 [B,Hkv,T,D/G]), bit-exact with the reference."""
+    _check_cuda4("v", v)
+    b, h, t, d = v.shape
+    assert d % group_size == 0, "this simple version assumes D_HEAD is a multiple of group_size"
+    v = v.contiguous()
+    packed = torch.empty((b, h, t, d // 4), dtype=torch.uint8, device=v.device)
+    scale = torch.empty((b, h, t, d // group_size), dtype=torch.float16, device=v.device)
+    zero = torch.empty_like(scale)
+    with torch.cuda.device(v.device):
+        _lib.check(_lib.load().nsa_kivi_quantize_v(v.data_ptr(), _dtype_code(v), packed.data_ptr(), scale.data_ptr(),
+                                                   zero.data_ptr(), b, h, t, d, group_size, bits,
+                                                   _lib.stream_handle(v.device)))
+    return packed, scale, zero
+
+
+def dequantize_k(packed, scale, zero_point, seq_len, tok_start=0, n_tokens=None):
+    """Dequantize K tokens [tok_start, tok_start + n_tokens) (positions clamped
+    to [0, seq_len)) -> float32 [B, Hkv, n_tokens, D]: ``s * (code - z)``."""
+    b, h, _, d = packed.shape
+    n = seq_len - tok_start if n_tokens is None else n_tokens
+    out = torch.empty((b, h, n, d), dtype=torch.float32, device=packed.device)
+    with torch.cuda.device(packed.device):
+        _lib.check(_lib.load().nsa_kivi_dequant_k(packed.contiguous().data_ptr(), scale.contiguous().data_ptr(),
+                                                  zero_point.contiguous().data_ptr(), out.data_ptr(), b, h, seq_len, d,
+                                                  tok_start, n, _lib.stream_handle(packed.device)))
+    return out
+
+
+def dequantize_v(packed, scale, zero_point, seq_len=None, tok_start=0, n_tokens=None):
+    """Dequantize V tokens [tok_start, tok_start + n_tokens) -> float32 [B, Hkv, n, D]."""
+    b, h, t, dp = packed.shape
+    seq_len = t if seq_len is None else seq_len
+    n = seq_len - tok_start if n_tokens is None else n_tokens
+    out = torch.empty((b, h, n, dp * 4), dtype=torch.float32, device=packed.device)
+    with torch.cuda.device(packed.device):
+        _lib.check(_lib.load().nsa_kivi_dequant_v(packed.contiguous().data_ptr(), scale.contiguous().data_ptr(),
+                                                  zero_point.contiguous().data_ptr(), out.data_ptr(), b, h, seq_len,
+                                                  dp * 4, tok_start, n, _lib.stream_handle(packed.device)))
+    return out
+
+
+def build_quantized_kv_cache(k_compacted, v_compacted, residual_size=RESIDUAL_SIZE, sink=SINK_SIZE):
+    """quant_kernel.py:584-622: slice a compacted [B, Hkv, S+W, D] cache into
+    the fp16 residual (last ``residual_size`` slots), the sink padded to one
+    group by repeating slot 0, and window-old [S, S+W-R); quantize the last two
+    on the GPU.  Returns the reference's 14-key dict."""
+    _check_cuda4("k_compacted", k_compacted)
+    n = k_compacted.shape[2]
+    win_end = n - residual_size
+    out = {
+        "k_residual": k_compacted[:, :, win_end:, :].contiguous(),
+        "v_residual": v_compacted[:, :, win_end:, :].contiguous(),
+    }
+    pad = GROUP_SIZE - sink
+
+    def _pad(x):
+        real = x[:, :, :sink, :]
+        return torch.cat([real, real[:, :, :1, :].expand(-1, -1, pad, -1)], dim=2).contiguous()
+
+    out["k_sink_packed"], out["k_sink_scale"], out["k_sink_zero"] = quantize_k_cache(_pad(k_compacted))
+    out["v_sink_packed"], out["v_sink_scale"], out["v_sink_zero"] = quantize_v_cache(_pad(v_compacted))
+    kw = k_compacted[:, :, sink:win_end, :].contiguous()
+    vw = v_compacted[:, :, sink:win_end, :].contiguous()
+    out["k_win_packed"], out["k_win_scale"], out["k_win_zero"] = quantize_k_cache(kw)
+    out["v_win_packed"], out["v_win_scale"], out["v_win_zero"] = quantize_v_cache(vw)
+    return out
+
+
+_KIVI_ORDER = ["k_sink_packed", "k_sink_scale", "k_sink_zero", "v_sink_packed", "v_sink_scale", "v_sink_zero",
+               "k_win_packed", "k_win_scale", "k_win_zero", "v_win_packed", "v_win_scale", "v_win_zero"]
+
+
+def sparse_decode_attention_quantized(q, k_cache, v_cache,
+                                      k_sink_packed, k_sink_scale, k_sink_zero,
+                                      v_sink_packed, v_sink_scale, v_sink_zero,
+                                      k_win_packed, k_win_scale, k_win_zero,
+                                      v_win_packed, v_win_scale, v_win_zero,
+                                      seq_len, window, sink=SINK_SIZE, residual_size=RESIDUAL_SIZE,
+                                      group_size=GROUP_SIZE, bits=QUANT_BITS, sm_scale=None):
+    """quant_kernel.py:551-581.  k_cache/v_cache are the fp16 RESIDUAL
+    [B, Hkv, residual_size, D]; the other 12 tensors as built by
+    build_quantized_kv_cache.  Requires window >= residual_size."""
+    _req(isinstance(q, torch.Tensor) and q.is_cuda, "q must be a CUDA tensor (no CPU fallback)")
+    _req(q.dtype == torch.float16, f"q must be float16, got {q.dtype}", TypeError)
+    _req(q.dim() == 3 and q.is_contiguous(), "q must be a contiguous [B, H, D] tensor")
+    b, h, d = q.shape
+    _req(d == D_HEAD, f"head_dim must be {D_HEAD}")
+    _req(k_cache.dtype == torch.float16 and v_cache.dtype == torch.float16, "residual caches must be float16",
+         TypeError)
+    hkv = k_cache.shape[1]
+    _req(tuple(k_cache.shape) == (b, hkv, residual_size, d) and v_cache.shape == k_cache.shape,
+         f"k_cache/v_cache must be [B, Hkv, residual_size={residual_size}, D]")
+    window, sink, seq_len = int(window), int(sink), int(seq_len)
+    tensors = [k_sink_packed, k_sink_scale, k_sink_zero, v_sink_packed, v_sink_scale, v_sink_zero,
+               k_win_packed, k_win_scale, k_win_zero, v_win_packed, v_win_scale, v_win_zero]
+    nw = window - residual_size
+    expect = [(b, hkv, GROUP_SIZE // 4, d), (b, hkv, 1, d), (b, hkv, 1, d),
+              (b, hkv, GROUP_SIZE, d // 4), (b, hkv, GROUP_SIZE, d // GROUP_SIZE), (b, hkv, GROUP_SIZE, d // GROUP_SIZE),
+              (b, hkv, max(nw, 0) // 4, d), (b, hkv, max(nw, 0) // GROUP_SIZE, d), (b, hkv, max(nw, 0) // GROUP_SIZE, d),
+              (b, hkv, max(nw, 0), d // 4), (b, hkv, max(nw, 0), d // GROUP_SIZE),
+              (b, hkv, max(nw, 0), d // GROUP_SIZE)]
+    for name, t, shp in zip(_KIVI_ORDER, tensors, expect):
+        _req(isinstance(t, torch.Tensor) and t.is_cuda and t.is_contiguous(), f"{name} must be a contiguous CUDA tensor")
+        _req(tuple(t.shape) == shp, f"{name} must have shape {shp}, got {tuple(t.shape)}")
+        _req(t.dtype == (torch.uint8 if name.endswith("packed") else torch.float16), f"{name} has wrong dtype {t.dtype}",
+             TypeError)
+    if sm_scale is None:
+        sm_scale = D_HEAD ** -0.5
+    o = torch.empty_like(q)
+    lib = _lib.load()
+    ws_bytes = lib.nsa_kivi_workspace_bytes(b, hkv, window, residual_size)
+    with torch.cuda.device(q.device):
+        ws = _lib.workspace(q.device, ws_bytes)
+        ptrs = [t.data_ptr() if t.numel() else None for t in tensors]
+        _lib.check(lib.nsa_kivi_decode(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), *ptrs, o.data_ptr(),
+                                       b, h, hkv, d, seq_len, window, sink, residual_size, group_size, bits,
+                                       float(sm_scale), ws.data_ptr(), ws.numel(), _lib.stream_handle(q.device)))
+    return o
+
+
+# --------------------------------------------------------------------------
+# streaming cache
+# --------------------------------------------------------------------------
+
+class KiviStreamCacheDesc(ctypes.Structure):
+    """ctypes mirror of nsa_kivi_stream_cache (include/nsa_b200.h)."""
+    _fields_ = [(n, ctypes.c_int64) for n in ("batch", "n_kv_heads", "head_dim", "window", "sink", "residual",
+                                              "n_groups")] + \
+               [(n, ctypes.c_void_p) for n in ("unit_lens", "sink_k", "sink_v",
+                                               "k_sink_packed", "k_sink_scale", "k_sink_zero",
+                                               "v_sink_packed", "v_sink_scale", "v_sink_zero",
+                                               "k_win_packed", "k_win_scale", "k_win_zero",
+                                               "v_win_packed", "v_win_scale", "v_win_zero", "k_res", "v_res")]
+
+
+class KiviCache:
+    """Streaming KIVI cache for one attention layer (see nsa_kivi_stream_cache).
+
+    Usage per decode step:  ``o = cache.decode_step(q, new_k, new_v)``
+    (append then attend), or ``cache.append(new_k, new_v)`` / ``cache.attend(q)``.
+    """
+
+    def __init__(self, batch, n_kv_heads, window, sink=SINK_SIZE, residual=RESIDUAL_SIZE, head_dim=D_HEAD,
+                 device=None):
+        _req(head_dim == D_HEAD, f"head_dim must be {D_HEAD}")
+        _req(1 <= sink <= GROUP_SIZE, "sink must be in [1, 32]")
+        _req(residual >= GROUP_SIZE and residual % GROUP_SIZE == 0, "residual must be a positive multiple of 32")
+        _req(window >= 0 and (window < residual or (window - residual) % GROUP_SIZE == 0),
+             "window - residual must be a multiple of 32")
+        device = torch.device(device if device is not None else "cuda")
+        _req(device.type == "cuda", "KiviCache lives on a CUDA device")
+        self.batch, self.n_kv_heads, self.window, self.sink, self.residual = batch, n_kv_heads, window, sink, residual
+        self.head_dim = head_dim
+        self.n_groups = (window - residual) // GROUP_SIZE if window >= residual else 0
+        self.res_cap = residual + GROUP_SIZE
+        self.device = device
+        b, h, d, ng = batch, n_kv_heads, head_dim, self.n_groups
+        f16, u8 = torch.float16, torch.uint8
+
+        def z(shape, dt):
+            return torch.zeros(shape, dtype=dt, device=device)
+
+        self.unit_lens = z((b, h), torch.int64)
+        self.sink_k, self.sink_v = z((b, h, sink, d), f16), z((b, h, sink, d), f16)
+        self.k_sink_packed, self.k_sink_scale, self.k_sink_zero = z((b, h, 8, d), u8), z((b, h, 1, d), f16), \
+            z((b, h, 1, d), f16)
+        self.v_sink_packed, self.v_sink_scale, self.v_sink_zero = z((b, h, 32, d // 4), u8), \
+            z((b, h, 32, d // 32), f16), z((b, h, 32, d // 32), f16)
+        self.k_win_packed, self.k_win_scale, self.k_win_zero = z((b, h, ng * 8, d), u8), z((b, h, ng, d), f16), \
+            z((b, h, ng, d), f16)
+        self.v_win_packed, self.v_win_scale, self.v_win_zero = z((b, h, ng * 32, d // 4), u8), \
+            z((b, h, ng * 32, d // 32), f16), z((b, h, ng * 32, d // 32), f16)
+        self.k_res, self.v_res = z((b, h, self.res_cap, d), f16), z((b, h, self.res_cap, d), f16)
+        self._desc = self._make_desc()
+        lib = _lib.load()
+        self._ws_bytes = lib.nsa_kivi_stream_workspace_bytes(ctypes.byref(self._desc))
+
+    # ---------------------------------------------------------------- plumbing
+    def _make_desc(self):
+        dsc = KiviStreamCacheDesc()
+        for n in ("batch", "n_kv_heads", "head_dim", "window", "sink", "residual", "n_groups"):
+            setattr(dsc, n, int(getattr(self, n)))
+        for n in ("unit_lens", "sink_k", "sink_v", "k_sink_packed", "k_sink_scale", "k_sink_zero", "v_sink_packed",
+                  "v_sink_scale", "v_sink_zero", "k_win_packed", "k_win_scale", "k_win_zero", "v_win_packed",
+                  "v_win_scale", "v_win_zero", "k_res", "v_res"):
+            t = getattr(self, n)
+            setattr(dsc, n, t.data_ptr() if t.numel() else None)
+        return dsc
+
+    def state(self) -> dict:
+        """The cache tensors (views, not copies)."""
+        return {n: getattr(self, n) for n in ("unit_lens", "sink_k", "sink_v", "k_sink_packed", "k_sink_scale",
+                                              "k_sink_zero", "v_sink_packed", "v_sink_scale", "v_sink_zero",
+                                              "k_win_packed", "k_win_scale", "k_win_zero", "v_win_packed",
+                                              "v_win_scale", "v_win_zero", "k_res", "v_res")}
+
+    @property
+    def seq_len(self) -> int:
+        return int(self.unit_lens[0, 0].item())
+
+    # ---------------------------------------------------------------- steps
+    def append(self, new_k, new_v):
+        """Append one token per sequence: new_k/new_v [B, Hkv, D] float16."""
+        shape = (self.batch, self.n_kv_heads, self.head_dim)
+        for name, t in (("new_k", new_k), ("new_v", new_v)):
+            _req(isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == torch.float16 and t.is_contiguous()
+                 and tuple(t.shape) == shape, f"{name} must be a contiguous float16 CUDA tensor of shape {shape}")
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.load().nsa_kivi_append(ctypes.byref(self._desc), new_k.data_ptr(), new_v.data_ptr(),
+                                                   _lib.stream_handle(self.device)))
+
+    def attend(self, q, sm_scale=None):
+        """Decode q [B, 8*Hkv, D] float16 against the cache -> o like q."""
+        _req(isinstance(q, torch.Tensor) and q.is_cuda and q.dtype == torch.float16 and q.is_contiguous()
+             and tuple(q.shape) == (self.batch, 8 * self.n_kv_heads, self.head_dim),
+             "q must be a contiguous float16 CUDA tensor [B, 8*Hkv, 128]")
+        if sm_scale is None:
+            sm_scale = self.head_dim ** -0.5
+        o = torch.empty_like(q)
+        with torch.cuda.device(self.device):
+            ws = _lib.workspace(self.device, self._ws_bytes)
+            _lib.check(_lib.load().nsa_kivi_stream_decode(ctypes.byref(self._desc), q.data_ptr(), o.data_ptr(),
+                                                          float(sm_scale), ws.data_ptr(), ws.numel(),
+                                                          _lib.stream_handle(self.device)))
+        return o
+
+    def decode_step(self, q, new_k, new_v, sm_scale=None):
+        """One decode step: quantize-on-append of the new token, then attend."""
+        self.append(new_k, new_v)
+        return self.attend(q, sm_scale)
+
+    # ---------------------------------------------------------------- filling
+    def load_state(self, seq_len, sink_k, sink_v, tail_k=None, tail_v=None, tail_start=None):
+        """Set the cache to its state after ``seq_len`` appends.
+
+        sink_k/sink_v: [B, Hkv, min(seq_len, sink), D] float16, positions
+        [0, min(seq_len, sink)).  tail_k/tail_v: [B, Hkv, n, D] float16 holding
+        positions [tail_start, tail_start + n), tail_start >= sink, covering
+        every stream position the state keeps (live window groups and the
+        residual).  Uses the GPU quantizers of the append path, so the result
+        equals appending the same tokens one by one."""
+        S, G, R, NG, C = self.sink, GROUP_SIZE, self.residual, self.n_groups, self.res_cap
+        n_stream = max(0, seq_len - S)
+        F = max(0, (n_stream - R) // G)
+        n_grp = min(F, NG)
+        ns = min(seq_len, S)
+        self.unit_lens.fill_(seq_len)
+        for t in (self.k_res, self.v_res, self.sink_k, self.sink_v):
+            t.zero_()
+        if ns:
+            _req(sink_k.shape[2] >= ns, f"sink_k must hold {ns} tokens")
+            kk, vv = sink_k[:, :, :ns], sink_v[:, :, :ns]
+            self.sink_k[:, :, :ns] = kk
+            self.sink_v[:, :, :ns] = vv
+            kp = torch.cat([kk, kk[:, :, :1].expand(-1, -1, G - ns, -1)], dim=2).contiguous()
+            vp = torch.cat([vv, vv[:, :, :1].expand(-1, -1, G - ns, -1)], dim=2).contiguous()
+            self.k_sink_packed[:], self.k_sink_scale[:], self.k_sink_zero[:] = quantize_k_cache(kp)
+            self.v_sink_packed[:], self.v_sink_scale[:], self.v_sink_zero[:] = quantize_v_cache(vp)
+
+        def tok(a, b):
+            _req(tail_k is not None and a >= tail_start and b <= tail_start + tail_k.shape[2],
+                 f"tail must cover positions [{a}, {b})")
+            return tail_k[:, :, a - tail_start:b - tail_start], tail_v[:, :, a - tail_start:b - tail_start]
+
+        if n_grp:
+            g0 = F - n_grp
+            kk, vv = tok(S + G * g0, S + G * F)
+            kp, ks, kz = quantize_k_cache(kk.contiguous())
+            vp, vs, vz = quantize_v_cache(vv.contiguous())
+            for j in range(n_grp):
+                slot = (g0 + j) % NG
+                self.k_win_packed[:, :, slot * 8:(slot + 1) * 8] = kp[:, :, j * 8:(j + 1) * 8]
+                self.k_win_scale[:, :, slot] = ks[:, :, j]
+                self.k_win_zero[:, :, slot] = kz[:, :, j]
+                self.v_win_packed[:, :, slot * G:(slot + 1) * G] = vp[:, :, j * G:(j + 1) * G]
+                self.v_win_scale[:, :, slot * G:(slot + 1) * G] = vs[:, :, j * G:(j + 1) * G]
+                self.v_win_zero[:, :, slot * G:(slot + 1) * G] = vz[:, :, j * G:(j + 1) * G]
+        if n_stream > G * F:
+            kk, vv = tok(S + G * F, seq_len)
+            idx = torch.arange(G * F, n_stream, device=self.device) % C
+            self.k_res[:, :, idx] = kk
+            self.v_res[:, :, idx] = vv
+
+    def load_history(self, k_hist, v_hist, seq_len):
+        """State after appending positions [0, seq_len) of k_hist/v_hist
+        ([B, Hkv, >= seq_len, D] float16)."""
+        S = self.sink
+        self.load_state(seq_len, k_hist[:, :, :S], v_hist[:, :, :S], k_hist[:, :, S:seq_len], v_hist[:, :, S:seq_len],
+                        tail_start=S)
+
+    def kept_positions(self, seq_len):
+        """Oldest stream position the state after ``seq_len`` appends keeps."""
+        S, G, R, NG = self.sink, GROUP_SIZE, self.residual, self.n_groups
+        n_stream = max(0, seq_len - S)
+        F = max(0, (n_stream - R) // G)
+        return S + G * (F - min(F, NG))
+
+    @classmethod
+    def synthetic(cls, batch, n_kv_heads, window, seq_len, sink=SINK_SIZE, residual=RESIDUAL_SIZE, device=None,
+                  generator=None, outlier_channels=4, outlier_factor=8.0):
+        """A cache in its state after ``seq_len`` appends of seeded N(0,1) fp16
+        tokens (K with ``outlier_channels`` of the 128 channels scaled by
+        ``outlier_factor``); only the positions the state keeps are drawn."""
+        c = cls(batch, n_kv_heads, window, sink, residual, device=device)
+        d = c.head_dim
+        lo = c.kept_positions(seq_len)
+        n_tail = max(0, seq_len - lo)
+        ns = min(seq_len, sink)
+        kt = torch.randn(batch, n_kv_heads, ns + n_tail, d, device=c.device, generator=generator)
+        vt = torch.randn(batch, n_kv_heads, ns + n_tail, d, device=c.device, generator=generator)
+        if outlier_channels:
+            ch = torch.randperm(d, device=c.device, generator=generator)[:outlier_channels]
+            kt[..., ch] *= outlier_factor
+        kt, vt = kt.half(), vt.half()
+        c.load_state(seq_len, kt[:, :, :ns], vt[:, :, :ns], kt[:, :, ns:], vt[:, :, ns:], tail_start=lo)
+        return c
