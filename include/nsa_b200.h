@@ -91,6 +91,22 @@ int nsa_sparse_decode(const void* q, const void* k_cache, const void* v_cache, v
                       void* workspace, size_t workspace_bytes, nsa_stream_t stream);
 
 
+/* Same computation as nsa_sparse_decode, but allocates nothing and takes no
+ * workspace.  No counterpart in the reference: it exists for callers that
+ * cannot call cudaMalloc (or any allocator) where they decode, e.g. a host
+ * runtime that reserves all device memory through its own pool, or a plain C
+ * caller without a device allocator.  The split-K scratch lives in a static
+ * 4 MiB device array inside this library (held by every GPU that loads it
+ * until exit); shapes whose scratch does not fit are rejected with
+ * NSA_ERR_UNSUPPORTED.  The first call on a device looks the array up and
+ * clears it -- make that call before any stream capture.  All calls on a
+ * device share the array: calls that overlap on the GPU race on it. */
+int nsa_sparse_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, void* o,
+                              int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+                              int64_t window, int64_t sink, int64_t seq_len,
+                              const int64_t* seq_lens, const int32_t* ring_heads, float sm_scale,
+                              nsa_stream_t stream);
+
 /* ------------------------------------------------------------------ KIVI
  * 2-bit KIVI quantization: K per channel over groups of 32 tokens, V per
  * token over groups of 32 channels, asymmetric, fp16 scale and zero point,

@@ -42,6 +42,7 @@ PROTOTYPES = {
     "nsa_sparse_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64]),
     "nsa_sparse_decode": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _F, _P, _SZ,
                                  _P]),
+    "nsa_sparse_decode_noalloc": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _F, _P]),
     "nsa_kivi_quantize_k": (_INT, [_P, _INT, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "nsa_kivi_quantize_v": (_INT, [_P, _INT, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "nsa_kivi_dequant_k": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),

@@ -10,6 +10,7 @@
 // shared-memory ring (and the 8x128 Q block of each piece into a 2-slot
 // ring); warps 0-3 each consume 16 tokens of every tile on the tensor cores.
 #include <cstdlib>
+#include <mutex>
 
 #include "attn_engine.cuh"
 #include "host_util.h"
@@ -454,6 +455,107 @@ int nsa_sparse_decode(const void* q, const void* k_cache, const void* v_cache, v
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   const Split s = plan(batch * n_kv_heads, window + sink);
   return launch(p, s, k_cache, v_cache, window + sink, workspace, workspace_bytes_, stream);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Sink + window decode that allocates nothing.
+//
+// Some callers cannot call cudaMalloc, or allocate through torch, at the point
+// where they decode: a host runtime that reserves all device memory up front
+// through its own pool and does not let libraries allocate, a plain C caller
+// that owns no device allocator, or a decode loop where an allocation (which
+// may synchronize the device) is not acceptable.  For them the split-K scratch
+// of nsa_sparse_decode (tickets and partial results) lives in the static
+// device array below instead of a caller-provided workspace.
+//
+// Facts a caller must know:
+// * The array is kNoAllocScratchBytes (4 MiB) per GPU, held by every GPU that
+//   loads this library until the process exits.  Shapes whose scratch does not
+//   fit are rejected with NSA_ERR_UNSUPPORTED before anything is launched.
+// * The first call on a device looks up the array's device address
+//   (cudaGetSymbolAddress) and clears it (cudaMemset); make that first call
+//   before any stream capture.  Later calls on the device do neither.
+// * Every call on a device shares the one array.  The kernel leaves the parts
+//   it used zeroed again, but calls that overlap on the GPU (different streams
+//   without ordering) race on it and may return wrong results.  After a call
+//   reported NSA_ERR_TIMEOUT through nsa_device_error, the array may hold
+//   stale tickets; the next first-use set-up does not run again, so such a
+//   process should not keep using this entry point.
+// ---------------------------------------------------------------------------
+namespace nsa {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {nullptr};
+
+// Device address of g_noalloc_scratch on the current device, set up (address
+// lookup + clear) on first use; nullptr (with a message recorded) on failure.
+void* noalloc_scratch() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    fail(NSA_ERR_CUDA, "no current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+      return nullptr;
+    }
+    e = cudaMemset(ptr, 0, kNoAllocScratchBytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+      cuda_fail(e, "clearing g_noalloc_scratch");
+      return nullptr;
+    }
+    g_noalloc_ptr[dev] = ptr;
+  }
+  return g_noalloc_ptr[dev];
+}
+
+}  // namespace
+}  // namespace nsa
+
+extern "C" {
+
+int nsa_sparse_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, void* o, int64_t batch,
+                              int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, int64_t window, int64_t sink,
+                              int64_t seq_len, const int64_t* seq_lens, const int32_t* ring_heads, float sm_scale,
+                              nsa_stream_t stream) {
+  clear_error();
+  int rc = check_common(q, k_cache, v_cache, o, batch, n_heads, n_kv_heads, head_dim);
+  if (rc) return rc;
+  if (window < 0 || sink < 0 || window + sink < 1 || window + sink > (int64_t(1) << 30))
+    return fail(NSA_ERR_INVALID, "need window, sink >= 0 and 1 <= window + sink <= 2^30");
+  if (seq_len < 0) return fail(NSA_ERR_INVALID, "seq_len must be >= 0");
+  const Split s = plan(batch * n_kv_heads, window + sink);
+  const size_t need = workspace_bytes(s);
+  if (need > kNoAllocScratchBytes)
+    return fail(NSA_ERR_UNSUPPORTED,
+                "this shape needs %zu bytes of split-K scratch; the allocation-free entry point has %zu "
+                "(use nsa_sparse_decode with a workspace)",
+                need, kNoAllocScratchBytes);
+  void* scratch = noalloc_scratch();
+  if (!scratch) return NSA_ERR_CUDA;
+  Params p{};
+  p.q = static_cast<const __half*>(q);
+  p.o = static_cast<__half*>(o);
+  p.n_kv_heads = static_cast<int>(n_kv_heads);
+  p.mode = kSparse;
+  p.seq_len = seq_len;
+  p.seq_lens = seq_lens;
+  p.ring_heads = ring_heads;
+  p.window = static_cast<int>(window);
+  p.sink = static_cast<int>(sink);
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  return launch(p, s, k_cache, v_cache, window + sink, scratch, kNoAllocScratchBytes, stream);
 }
 
 }  // extern "C"
