@@ -284,11 +284,7 @@ def main():
             torch.distributed.barrier()
 
     def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], device=dev, dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        return float(t.item())
+        return importlib.import_module("numerics-and-sparse-attn_b200.shard").max_over_ranks(x, dev)
 
     with torch.cuda.stream(stream):
         for i in range(a.warmup):
@@ -361,13 +357,16 @@ def main():
         e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
         derr = wlobj.pkg.device_error(dev)
 
-    # verification outside the timed region: assemble all ranks' outputs
+    # verification outside the timed region: assemble all ranks' outputs with
+    # one all-gather (NCCL over NVLink) and check each rank's slice came back
     verified = bool(torch.isfinite(wlobj.out[0].float()).all().item()) and derr == 0
     if world > 1:
+        shard = importlib.import_module("numerics-and-sparse-attn_b200.shard")
         mine = wlobj.out[0].contiguous()
-        allo = torch.empty((world,) + tuple(mine.shape), dtype=mine.dtype, device=dev)
-        torch.distributed.all_gather_into_tensor(allo, mine)
-        verified = verified and bool(torch.isfinite(allo.float()).all().item()) and torch.equal(allo[rank], mine)
+        full = shard.gather_outputs(mine, B_PER_GPU * world, HKV)
+        sh = shard.shard_units(B_PER_GPU * world, HKV, world, rank)
+        verified = verified and bool(torch.isfinite(full.float()).all().item()) and \
+            torch.equal(sh.q_slice(full), mine)
         flag = torch.tensor([1.0 if verified else 0.0], device=dev)
         torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MIN)
         verified = flag.item() == 1.0
