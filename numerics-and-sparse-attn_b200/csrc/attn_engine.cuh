@@ -228,50 +228,51 @@ __device__ __forceinline__ void store_half4(__half* dst, const float (&o)[4]) {
 
 // Split-K partials of one unit: `n` pieces, each [8 heads] lse and
 // [8 heads][128] normalized outputs.  Log-sum-exp combine with warp shuffles:
-// consumer warp w reduces head w; lanes hold pieces for the max / sum, then 4
-// dims each for the weighted output sum.  Reads use ld.global.cg (the
-// partials were written by other SMs); every partial read is zeroed again so
-// the workspace is all-zero between launches whatever its next layout.
-__device__ __forceinline__ void combine_pieces(float* part_lse, float* part_o, int n, __half* out, int warp,
-                                               int lane) {
-  static_assert(kConsumerWarps == kGroupHeads, "one consumer warp per head");
-  const int head = warp;
-  float M = -INFINITY;
-  for (int i = lane; i < n; i += 32) M = fmaxf(M, __ldcg(part_lse + i * kGroupHeads + head));
+// the calling warp reduces heads [head0, head0 + n_heads); lanes hold pieces
+// for the max / sum, then 4 dims each for the weighted output sum.  Reads use
+// ld.global.cg (the partials were written by other SMs); every partial read
+// is zeroed again so the workspace is all-zero between launches whatever its
+// next layout.
+__device__ __forceinline__ void combine_pieces(float* part_lse, float* part_o, int n, __half* out, int head0,
+                                               int n_heads, int lane) {
+  for (int head = head0; head < head0 + n_heads; ++head) {
+    float M = -INFINITY;
+    for (int i = lane; i < n; i += 32) M = fmaxf(M, __ldcg(part_lse + i * kGroupHeads + head));
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  float W = 0.f;
-  for (int i = lane; i < n; i += 32) {
-    const float x = __ldcg(part_lse + i * kGroupHeads + head);
-    W += (x == -INFINITY) ? 0.f : fast_exp2(x - M);
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) W += __shfl_xor_sync(0xffffffffu, W, off);
-  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int base = 0; base < n; base += 32) {
-    const int i = base + lane;
-    const float x = (i < n) ? __ldcg(part_lse + i * kGroupHeads + head) : -INFINITY;
-    const float wi = (x == -INFINITY) ? 0.f : fast_exp2(x - M);
-    const int cnt = min(32, n - base);
-    for (int j = 0; j < cnt; ++j) {
-      const float wj = __shfl_sync(0xffffffffu, wi, j);
-      float4* src = reinterpret_cast<float4*>(part_o + ((base + j) * kGroupHeads + head) * kHeadDim) + lane;
-      if (wj != 0.f) {
-        const float4 v = __ldcg(src);
-        a.x += wj * v.x;
-        a.y += wj * v.y;
-        a.z += wj * v.z;
-        a.w += wj * v.w;
-      }
-      __stcg(src, make_float4(0.f, 0.f, 0.f, 0.f));
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float W = 0.f;
+    for (int i = lane; i < n; i += 32) {
+      const float x = __ldcg(part_lse + i * kGroupHeads + head);
+      W += (x == -INFINITY) ? 0.f : fast_exp2(x - M);
     }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) W += __shfl_xor_sync(0xffffffffu, W, off);
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int base = 0; base < n; base += 32) {
+      const int i = base + lane;
+      const float x = (i < n) ? __ldcg(part_lse + i * kGroupHeads + head) : -INFINITY;
+      const float wi = (x == -INFINITY) ? 0.f : fast_exp2(x - M);
+      const int cnt = min(32, n - base);
+      for (int j = 0; j < cnt; ++j) {
+        const float wj = __shfl_sync(0xffffffffu, wi, j);
+        float4* src = reinterpret_cast<float4*>(part_o + ((base + j) * kGroupHeads + head) * kHeadDim) + lane;
+        if (wj != 0.f) {
+          const float4 v = __ldcg(src);
+          a.x += wj * v.x;
+          a.y += wj * v.y;
+          a.z += wj * v.z;
+          a.w += wj * v.w;
+        }
+        __stcg(src, make_float4(0.f, 0.f, 0.f, 0.f));
+      }
+    }
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) __stcg(part_lse + i * kGroupHeads + head, 0.f);
+    const float inv = __fdividef(1.f, W);  // W == 0 (no valid token anywhere) -> inf * 0 = NaN, as the reference's 0/0
+    __half2* dst = reinterpret_cast<__half2*>(out + head * kHeadDim + lane * 4);
+    dst[0] = __floats2half2_rn(a.x * inv, a.y * inv);
+    dst[1] = __floats2half2_rn(a.z * inv, a.w * inv);
   }
-  __syncwarp();
-  for (int i = lane; i < n; i += 32) __stcg(part_lse + i * kGroupHeads + head, 0.f);
-  const float inv = __fdividef(1.f, W);  // W == 0 (no valid token anywhere) -> inf * 0 = NaN, as the reference's 0/0
-  __half2* dst = reinterpret_cast<__half2*>(out + head * kHeadDim + lane * 4);
-  dst[0] = __floats2half2_rn(a.x * inv, a.y * inv);
-  dst[1] = __floats2half2_rn(a.z * inv, a.w * inv);
 }
 
 }  // namespace nsa

@@ -9,6 +9,7 @@
 // combine.  Per CTA: warp 4 issues TMA loads of K/V tiles into a 6-stage
 // shared-memory ring (and the 8x128 Q block of each piece into a 2-slot
 // ring); warps 0-3 each consume 16 tokens of every tile on the tensor cores.
+#include <cstddef>
 #include <cstdlib>
 #include <mutex>
 
@@ -48,6 +49,9 @@ struct Smem {
   uint64_t q_full[2];
   uint64_t q_empty[2];
 };
+
+static_assert(offsetof(Smem, kv) % 1024 == 0 && kStageBytes % 1024 == 0, "TMA tile destinations");
+static_assert(offsetof(Smem, q) % 16 == 0 && kQBytes % 16 == 0, "bulk-copy destinations");
 
 enum Mode : int { kDense = 0, kSparse = 1 };
 
@@ -277,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __threadfence();
         const int64_t base = pc.unit * p.max_pieces;
         combine_pieces(p.part_lse + base * kGroupHeads, p.part_o + base * kGroupHeads * kHeadDim, pc.n_pieces, out,
-                       warp, lane);
+                       warp * kGroupHeads / kConsumerWarps, kGroupHeads / kConsumerWarps, lane);
         if (ct == 0) p.counters[pc.unit] = 0;  // ready for the next launch
       }
     }

@@ -3,19 +3,28 @@
 // ring layout of nsa_kivi_stream_cache.
 //
 // Per (batch, kv_head) unit the work is a fixed list of items:
-//   Q-batches  up to 8 quantized 32-token groups (slot 0 of batch 0 is the
-//              padded sink group, then window groups in physical order),
-//              staged into shared memory with 1-D bulk copies (3 KiB/group);
 //   F-tiles    64 slots of the fp16 residual (ring), staged by TMA with the
-//              128-byte swizzle exactly like the fp16 kernel.
-// Items that hold no attended token are skipped by producer and consumers
-// alike (both derive it from the same per-unit metadata).  Consumers: two
-// groups of 4 warps take alternate items.  For a Q-batch each warp
-// dequantizes 16-token halves of groups into a private fp16 tile (swizzled
-// like a TMA tile; unattended tokens are written as zeros) and runs the same
-// mma.sync engine on it, so both regimes accumulate into one online softmax.
-// Split-K / unit-aligned scheduling and the in-launch combine are the fp16
-// kernel's.
+//              128-byte swizzle (F ring, 3 x 32 KiB);
+//   Q-batches  up to 6 quantized 32-token groups (slot 0 of batch 0 is the
+//              padded sink group, then window groups in physical order),
+//              staged with 1-D bulk copies, 3 KiB per group (Q ring, 2 x 18 KiB).
+// Items holding no attended token are skipped by every role alike (all derive
+// it from the same per-unit metadata).
+//
+// Warp roles (warp specialization):
+//   warp 8      producer: issues the loads of both rings;
+//   warps 4-7   dequantizers: each turns whole quantized groups (round-robin)
+//               into swizzled fp16 K/V tiles in its own DQ slot, writing
+//               zeros for unattended V rows;
+//   warps 0-3   MMA warps: consume fp16 tiles -- residual tiles straight from
+//               the F ring (warp w takes rows 16w..16w+15) and dequantized
+//               groups from the DQ ring (16-token halves round-robin) -- with
+//               the shared mma.sync engine, then run the epilogue.
+// Dequantization thus overlaps the tensor-core work and the loads instead of
+// sitting in front of them.  Every ring has all of its consumers wait on every
+// phase, as parity waits require.  Scheduling (whole units per CTA, or
+// stream-K with the in-launch combine) is the fp16 kernel's.
+#include <cstddef>
 #include <cstdlib>
 
 #include "attn_engine.cuh"
@@ -24,18 +33,29 @@
 namespace nsa {
 namespace {
 
-constexpr int kStages = 4;
-static_assert(kStages % kGroups == 0, "each stage must belong to one consumer group");
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kMmaWarps = 4;
+constexpr int kDqWarps = 4;
+constexpr int kProducerWarp = kMmaWarps + kDqWarps;
+constexpr int kThreads = (kProducerWarp + 1) * 32;
+constexpr int kFStages = 3;
+constexpr int kQStages = 2;
+// One DQ slot per dequantizer: a slot then alternates strictly between its
+// own warp's production and the MMA warps' release, so a parity wait on it can
+// never be two phases behind (a slot shared by independent producers could).
+constexpr int kDqSlots = kDqWarps;
 constexpr uint32_t kRegionBytes = kTile * 128;
 constexpr uint32_t kTileBytes = 2 * kRegionBytes;
-constexpr uint32_t kStageBytes = 2 * kTileBytes;  // 32 KiB
+constexpr uint32_t kFStageBytes = 2 * kTileBytes;  // 32 KiB: K + V of 64 slots
 constexpr uint32_t kQBytes = kGroupHeads * kHeadDim * 2;
-constexpr int kBatchGroups = 8;                   // quantized groups per Q-batch
+constexpr int kBatchGroups = 6;                    // quantized groups per Q-batch
 // Q-batch stage layout (byte offsets); one slot per group
-constexpr uint32_t kOffKP = 0, kOffKS = 8192, kOffKZ = 10240, kOffVP = 12288, kOffVS = 20480, kOffVZ = 22528;
-constexpr uint32_t kScratchRegion = 16 * 128;     // 16 rows x 64 dims fp16
-constexpr uint32_t kScratchTile = 2 * kScratchRegion;
+constexpr uint32_t kOffKP = 0, kOffKS = kBatchGroups * 1024, kOffKZ = kOffKS + kBatchGroups * 256,
+                   kOffVP = kOffKZ + kBatchGroups * 256, kOffVS = kOffVP + kBatchGroups * 1024,
+                   kOffVZ = kOffVS + kBatchGroups * 256;
+constexpr uint32_t kQStageBytes = kOffVZ + kBatchGroups * 256;  // 3 KiB per group
+constexpr uint32_t kDqRegion = 32 * 128;           // 32 rows x 64 dims fp16
+constexpr uint32_t kDqTile = 2 * kDqRegion;        // K (or V) of one group
+constexpr uint32_t kDqSlotBytes = 2 * kDqTile;     // K + V, 16 KiB
 
 struct KiviMeta {
   int32_t n_sink;    // attended sink tokens
@@ -48,17 +68,32 @@ struct KiviMeta {
   int32_t pad;
 };
 
-struct Smem {
-  uint8_t stage[kStages][kStageBytes];  // 1024-aligned
-  uint8_t scratch[kConsumerWarps][2][kScratchTile];
-  uint8_t q[2][kQBytes];
-  KiviMeta meta[2];
-  EpilogueSmem ep;
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
-  uint64_t q_full[2];
-  uint64_t q_empty[2];
+struct QHeader {  // written by the producer into each Q-ring stage
+  KiviMeta meta;
+  int32_t item;  // Q-batch index within its unit
+  int32_t end;   // 1: no more work (sentinel for the dequantizers)
 };
+
+struct Smem {
+  // copy destinations first: every one stays 16-byte (TMA tiles: 1024-byte) aligned
+  uint8_t f[kFStages][kFStageBytes];  // 1024-aligned
+  uint8_t dq[kDqSlots][kDqSlotBytes];
+  uint8_t qb[kQStages][kQStageBytes];
+  uint8_t q[2][kQBytes];
+  EpilogueSmem ep;
+  QHeader qhdr[kQStages];
+  KiviMeta meta[2];
+  uint32_t dq_mask[kDqSlots];         // attended tokens of the group in each DQ slot
+  uint64_t f_full[kFStages], f_empty[kFStages];
+  uint64_t q_full[kQStages], q_empty[kQStages];
+  uint64_t dq_full[kDqSlots], dq_empty[kDqSlots];
+  uint64_t qv_full[2], qv_empty[2];
+};
+
+static_assert(offsetof(Smem, f) % 1024 == 0 && kFStageBytes % 1024 == 0, "TMA tile destinations");
+static_assert(offsetof(Smem, qb) % 16 == 0 && kQStageBytes % 16 == 0, "bulk-copy destinations");
+static_assert(offsetof(Smem, q) % 16 == 0 && kQBytes % 16 == 0, "bulk-copy destinations");
+static_assert(offsetof(Smem, dq) % 128 == 0, "dequantized tiles");
 
 struct KParams {
   const __half* q;
@@ -136,15 +171,6 @@ __device__ __forceinline__ int grp_age(const KParams& p, const KiviMeta& m, int 
   int d = gp - m.grp_head;
   if (d < 0) d += p.n_groups;
   return d;
-}
-
-// Attended token j (0..31) of batch slot `slot` of Q-batch `b`?
-__device__ __forceinline__ bool q_token_valid(const KParams& p, const KiviMeta& m, int b, int slot, int j) {
-  const int v = kBatchGroups * b + slot;
-  if (v == 0) return j < m.n_sink;
-  if (v > p.n_groups) return false;
-  const int age = grp_age(p, m, v - 1);
-  return age < m.n_grp && 32 * age + j >= m.tok_skip;
 }
 
 __device__ __forceinline__ bool q_slot_live(const KParams& p, const KiviMeta& m, int b, int slot) {
@@ -230,108 +256,92 @@ struct PieceIter {
 __device__ __forceinline__ __half2 u32_as_h2(uint32_t x) { return *reinterpret_cast<__half2*>(&x); }
 __device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-// Dequantize K of 16 tokens (half `hf` of batch slot `slot`) into a swizzled
-// [2][16][64] fp16 tile.  Lane = (byte row br = lane/8: tokens 4br..4br+3,
-// channel chunk cc = lane%8: channels 16cc..16cc+15).
-__device__ __forceinline__ void dequant_k16(uint32_t stage, uint32_t dst, int slot, int hf, int lane,
-                                            uint32_t valid_mask /* bit t: token t (0..15) attended */) {
-  const int br = lane >> 3, cc = lane & 7;
-  uint4 codes;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(codes.x), "=r"(codes.y), "=r"(codes.z), "=r"(codes.w)
-               : "r"(stage + kOffKP + slot * 1024 + (4 * hf + br) * 128 + 16 * cc));
-  uint32_t sc[8], zr[8];
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(sc[0]), "=r"(sc[1]), "=r"(sc[2]), "=r"(sc[3])
-               : "r"(stage + kOffKS + slot * 256 + 32 * cc));
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(sc[4]), "=r"(sc[5]), "=r"(sc[6]), "=r"(sc[7])
-               : "r"(stage + kOffKS + slot * 256 + 32 * cc + 16));
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(zr[0]), "=r"(zr[1]), "=r"(zr[2]), "=r"(zr[3])
-               : "r"(stage + kOffKZ + slot * 256 + 32 * cc));
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(zr[4]), "=r"(zr[5]), "=r"(zr[6]), "=r"(zr[7])
-               : "r"(stage + kOffKZ + slot * 256 + 32 * cc + 16));
-  __half2 s2[8], nz2[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    s2[i] = u32_as_h2(sc[i]);
-    nz2[i] = __hneg2(__hmul2(s2[i], u32_as_h2(zr[i])));
-  }
-  const uint32_t w[4] = {codes.x, codes.y, codes.z, codes.w};
-  const __half2 k1024 = u32_as_h2(0x64006400u);
-  // region of channels 16cc..: cc/4; chunks 2cc, 2cc+1 (mod 8).  Lanes with
-  // cc >= 4 store the second chunk first so a phase spreads over all banks.
-  const uint32_t region = dst + (cc >> 2) * kScratchRegion;
-  const uint32_t ch0 = (2 * cc) & 7;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int row = 4 * br + j;
-    const bool ok = (valid_mask >> row) & 1u;
-    uint32_t out[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t x = __byte_perm(w[i >> 1], 0u, (i & 1) ? 0x4342u : 0x4140u);  // [b_lo, 0, b_hi, 0]
-      const uint32_t c = ((x >> (2 * j)) & 0x00030003u) | 0x64006400u;
-      const __half2 v = __hfma2(__hsub2(u32_as_h2(c), k1024), s2[i], nz2[i]);
-      out[i] = ok ? h2_as_u32(v) : 0u;
-    }
-    const bool swap = (cc >> 2) & 1;
-    const uint32_t a0 = region + swz128(row, swap ? ch0 + 1 : ch0);
-    const uint32_t a1 = region + swz128(row, swap ? ch0 : ch0 + 1);
-    uint32_t f[4], sc2[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      f[i] = swap ? out[4 + i] : out[i];
-      sc2[i] = swap ? out[i] : out[4 + i];
-    }
-    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a0), "r"(f[0]), "r"(f[1]), "r"(f[2]), "r"(f[3]));
-    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a1), "r"(sc2[0]), "r"(sc2[1]), "r"(sc2[2]),
-                 "r"(sc2[3]));
-  }
+__device__ __forceinline__ void lds128(uint32_t a, uint32_t& x, uint32_t& y, uint32_t& z, uint32_t& w) {
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(x), "=r"(y), "=r"(z), "=r"(w) : "r"(a));
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w));
 }
 
-// Dequantize V of 16 tokens into a swizzled [2][16][64] fp16 tile.
-// Lane = (token tau = lane/2, channel half hv = lane%2: channels 64hv..+63).
-__device__ __forceinline__ void dequant_v16(uint32_t stage, uint32_t dst, int slot, int hf, int lane,
-                                            uint32_t valid_mask) {
-  const int tau = lane >> 1, hv = lane & 1;
-  const int trow = 16 * hf + tau;  // token within the 32-token group
-  uint4 codes;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(codes.x), "=r"(codes.y), "=r"(codes.z), "=r"(codes.w)
-               : "r"(stage + kOffVP + slot * 1024 + trow * 32 + 16 * hv));
-  uint32_t sc, zr;  // groups 2hv, 2hv+1 of this token
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(sc) : "r"(stage + kOffVS + slot * 256 + trow * 8 + 4 * hv));
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(zr) : "r"(stage + kOffVZ + slot * 256 + trow * 8 + 4 * hv));
-  const __half2 s_pair = u32_as_h2(sc), z_pair = u32_as_h2(zr);
-  const __half2 nz_pair = __hneg2(__hmul2(s_pair, z_pair));
-  const bool ok = (valid_mask >> tau) & 1u;
+// Dequantize one 32-token group (batch slot `slot` of the Q stage at `qs`)
+// into the DQ slot at `dst`: K tile [2][32 rows][64 dims] then V tile, both
+// swizzled like a TMA tile, rows in token order.  V rows of unattended tokens
+// (bit clear in `valid`) are written as zeros so that stale or degenerate
+// data (an fp16 zero point that overflowed to inf) cannot reach P.V.
+__device__ __forceinline__ void dequant_group(uint32_t qs, int slot, uint32_t dst, uint32_t valid, int lane) {
   const __half2 k1024 = u32_as_h2(0x64006400u);
-  const __half2 quarter_hi = __halves2half2(__float2half_rn(1.f), __float2half_rn(0.25f));
-  const uint32_t region = dst + hv * kScratchRegion;
-  // The two lanes of a token write chunks ch and ch ^ 4 at the same time
-  // (different banks); chunk ch = channels 8ch..8ch+7 of this half = bytes
-  // 2ch, 2ch+1 of the loaded 16; its channel group is ch / 4.
+  {
+    // K: lane = (byte row r: tokens 4r..4r+3, channel quarter cq: 32 channels)
+    const int r = lane >> 2, cq = lane & 3;
+    uint32_t w[8], sc[16], zr[16];
+    const uint32_t src = qs + kOffKP + slot * 1024 + r * 128 + 32 * cq;
+    lds128(src, w[0], w[1], w[2], w[3]);
+    lds128(src + 16, w[4], w[5], w[6], w[7]);
 #pragma unroll
-  for (int ci = 0; ci < 8; ++ci) {
-    const int ch = ci ^ (hv << 2);
-    const uint32_t wsel = (ch < 2) ? codes.x : (ch < 4) ? codes.y : (ch < 6) ? codes.z : codes.w;
-    const __half2 s = (ch < 4) ? __low2half2(s_pair) : __high2half2(s_pair);
-    const __half2 nz = (ch < 4) ? __low2half2(nz_pair) : __high2half2(nz_pair);
-    uint32_t out[4];
-#pragma unroll
-    for (int bb = 0; bb < 2; ++bb) {
-      const uint32_t k = (2 * ch + bb) & 3;
-      const uint32_t x = __byte_perm(wsel, 0u, 0x4040u | (k << 8) | k);  // [b, 0, b, 0]
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        // channels (4 byte + 2hh, +1): bits 4hh..4hh+1 (lo) and 4hh+2..+3 (hi, scaled by 4)
-        const uint32_t c = ((x >> (4 * hh)) & 0x000C0003u) | 0x64006400u;
-        const __half2 cv = __hmul2(__hsub2(u32_as_h2(c), k1024), quarter_hi);
-        const __half2 v = __hfma2(cv, s, nz);
-        out[2 * bb + hh] = ok ? h2_as_u32(v) : 0u;
-      }
+    for (int i = 0; i < 4; ++i) {
+      lds128(qs + kOffKS + slot * 256 + 64 * cq + 16 * i, sc[4 * i], sc[4 * i + 1], sc[4 * i + 2], sc[4 * i + 3]);
+      lds128(qs + kOffKZ + slot * 256 + 64 * cq + 16 * i, zr[4 * i], zr[4 * i + 1], zr[4 * i + 2], zr[4 * i + 3]);
     }
-    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(region + swz128(tau, ch)), "r"(out[0]), "r"(out[1]),
-                 "r"(out[2]), "r"(out[3]));
+    uint32_t x[16];
+    __half2 nz[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      x[i] = __byte_perm(w[i >> 1], 0u, (i & 1) ? 0x4342u : 0x4140u);  // [b_lo, 0, b_hi, 0]
+      nz[i] = __hneg2(__hmul2(u32_as_h2(sc[i]), u32_as_h2(zr[i])));
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t row = 4 * r + j;
+      uint32_t out[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t c = ((x[i] >> (2 * j)) & 0x00030003u) | 0x64006400u;
+        out[i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(c), k1024), u32_as_h2(sc[i]), nz[i]));
+      }
+      // channels 32cq.. = global chunks 4cq..4cq+3: region cq/2, local chunks (4cq & 7)..
+      const uint32_t region = dst + (cq >> 1) * kDqRegion;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc)
+        sts128(region + swz128(row, ((4 * cq) & 7) + cc), out[4 * cc], out[4 * cc + 1], out[4 * cc + 2],
+               out[4 * cc + 3]);
+    }
+  }
+  {
+    // V: lane = token (channels in bytes: byte b holds channels 4b..4b+3)
+    const int tau = lane;
+    const bool ok = (valid >> tau) & 1u;
+    uint32_t w[8];
+    const uint32_t src = qs + kOffVP + slot * 1024 + tau * 32;
+    lds128(src, w[0], w[1], w[2], w[3]);
+    lds128(src + 16, w[4], w[5], w[6], w[7]);
+    uint32_t s01, s23, z01, z23;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(s01), "=r"(s23) : "r"(qs + kOffVS + slot * 256 + tau * 8));
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(z01), "=r"(z23) : "r"(qs + kOffVZ + slot * 256 + tau * 8));
+    const __half2 sp[2] = {u32_as_h2(s01), u32_as_h2(s23)};
+    const __half2 nzp[2] = {__hneg2(__hmul2(sp[0], u32_as_h2(z01))), __hneg2(__hmul2(sp[1], u32_as_h2(z23)))};
+    const __half2 quarter_hi = __halves2half2(__float2half_rn(1.f), __float2half_rn(0.25f));
+    const uint32_t vdst = dst + kDqTile;
+#pragma unroll
+    for (int ch = 0; ch < 16; ++ch) {  // 8 channels = bytes 2ch, 2ch+1; group ch / 4
+      const int q = ch >> 2;
+      const __half2 s = (q & 1) ? __high2half2(sp[q >> 1]) : __low2half2(sp[q >> 1]);
+      const __half2 nzq = (q & 1) ? __high2half2(nzp[q >> 1]) : __low2half2(nzp[q >> 1]);
+      uint32_t out[4];
+#pragma unroll
+      for (int bb = 0; bb < 2; ++bb) {
+        const int byte = 2 * ch + bb;
+        const uint32_t k = byte & 3;
+        const uint32_t xb = __byte_perm(w[byte >> 2], 0u, 0x4040u | (k << 8) | k);  // [b, 0, b, 0]
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          // channels 4 byte + 2hh, +1: bits 4hh..+1 (lo) and 4hh+2..+3 (hi, as 4c)
+          const uint32_t c = ((xb >> (4 * hh)) & 0x000C0003u) | 0x64006400u;
+          const __half2 cv = __hmul2(__hsub2(u32_as_h2(c), k1024), quarter_hi);
+          out[2 * bb + hh] = ok ? h2_as_u32(__hfma2(cv, s, nzq)) : 0u;
+        }
+      }
+      sts128(vdst + (ch >> 3) * kDqRegion + swz128(tau, ch & 7), out[0], out[1], out[2], out[3]);
+    }
   }
 }
 
@@ -357,6 +367,25 @@ __device__ __forceinline__ void zero_invalid_v_rows(uint32_t vbase, uint32_t reg
   __syncwarp();
 }
 
+__device__ __forceinline__ void mma_warps_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kMmaWarps * 32) : "memory");
+}
+
+// Attended-token mask (bit j = token j) of batch slot `slot` of Q-batch `b`.
+__device__ __forceinline__ uint32_t group_mask(const KParams& p, const KiviMeta& m, int b, int slot) {
+  uint32_t mask = 0;
+  const int v = kBatchGroups * b + slot;
+  if (v == 0) return m.n_sink >= 32 ? 0xffffffffu : ((1u << m.n_sink) - 1u);
+  if (v > p.n_groups) return 0;
+  const int age = grp_age(p, m, v - 1);
+  if (age >= m.n_grp) return 0;
+  const int first = m.tok_skip - 32 * age;  // tokens below this one are not attended
+  if (first <= 0) return 0xffffffffu;
+  if (first >= 32) return 0;
+  mask = ~((1u << first) - 1u);
+  return mask;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     kivi_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                        const KParams p) {
@@ -365,194 +394,247 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(smem_u32(&sm.full[s]), 1);
-      mbar_init(smem_u32(&sm.empty[s]), kGroupWarps);
+    for (int s = 0; s < kFStages; ++s) {
+      mbar_init(smem_u32(&sm.f_full[s]), 1);
+      mbar_init(smem_u32(&sm.f_empty[s]), kMmaWarps);
+    }
+    for (int s = 0; s < kQStages; ++s) {
+      mbar_init(smem_u32(&sm.q_full[s]), 1);
+      mbar_init(smem_u32(&sm.q_empty[s]), kDqWarps);
+    }
+    for (int s = 0; s < kDqSlots; ++s) {
+      mbar_init(smem_u32(&sm.dq_full[s]), 1);
+      mbar_init(smem_u32(&sm.dq_empty[s]), kMmaWarps);
     }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(smem_u32(&sm.q_full[s]), 1);
-      mbar_init(smem_u32(&sm.q_empty[s]), kConsumerWarps);
+      mbar_init(smem_u32(&sm.qv_full[s]), 1);
+      mbar_init(smem_u32(&sm.qv_empty[s]), kMmaWarps);
     }
     fence_barrier_init();
   }
   __syncthreads();
 
-  // CTA-local live item k lives in stage k % kStages, phase (k / kStages) & 1,
-  // and is consumed by group k % kGroups.
-  if (warp == kConsumerWarps) {
+  if (warp == kProducerWarp) {
     // ---------------------------------------------------------- producer
     if (lane == 0) {
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
-      int qs = 0;
-      uint32_t qphase = 0, k = 0;
+      uint32_t nf = 0, nq = 0, nv = 0;  // items issued per ring
       PieceIter it(p);
       Piece pc;
-      while (it.next(p, pc)) {
-        if (!mbar_wait(smem_u32(&sm.q_empty[qs]), qphase ^ 1, p.err)) return;
-        const KiviMeta meta = make_meta(p, pc.unit);
-        sm.meta[qs] = meta;  // published by the arrive below (release)
-        mbar_arrive_expect_tx(smem_u32(&sm.q_full[qs]), kQBytes);
-        bulk_load(smem_u32(sm.q[qs]), p.q + pc.unit * kGroupHeads * kHeadDim, kQBytes, smem_u32(&sm.q_full[qs]));
-        if (++qs == 2) { qs = 0; qphase ^= 1; }
+      bool ok = true;
+      while (ok && it.next(p, pc)) {
         const int64_t u = pc.unit;
-        for (int64_t t = pc.t_begin; t < pc.t_end; ++t) {
-          const int itm = static_cast<int>(t);
-          if (!item_live(p, meta, itm)) continue;
-          const uint32_t stage = k % kStages, phase = (k / kStages) & 1;
-          ++k;
-          if (!mbar_wait(smem_u32(&sm.empty[stage]), phase ^ 1, p.err)) return;
-          const uint32_t fb = smem_u32(&sm.full[stage]);
-          const uint32_t sd = smem_u32(sm.stage[stage]);
-          if (itm < p.n_qb) {
-            // Q-batch: sink group (slot 0 of batch 0) + window groups [p0, p1)
-            const int b = itm;
-            const bool has_sink = (b == 0);
-            const int p0 = b == 0 ? 0 : kBatchGroups * b - 1;
-            const int p1 = min(p.n_groups, kBatchGroups * b + kBatchGroups - 1);
-            const int so = p0 + 1 - kBatchGroups * b;  // batch slot of group p0
-            const uint32_t ng = p1 > p0 ? p1 - p0 : 0;
-            const uint32_t bytes = (has_sink ? 3072u : 0u) + ng * 3072u;
-            mbar_arrive_expect_tx(fb, bytes);
-            if (has_sink) {
-              bulk_load(sd + kOffKP, p.ks_p + u * 1024, 1024, fb);
-              bulk_load(sd + kOffKS, p.ks_s + u * 128, 256, fb);
-              bulk_load(sd + kOffKZ, p.ks_z + u * 128, 256, fb);
-              bulk_load(sd + kOffVP, p.vs_p + u * 1024, 1024, fb);
-              bulk_load(sd + kOffVS, p.vs_s + u * 128, 256, fb);
-              bulk_load(sd + kOffVZ, p.vs_z + u * 128, 256, fb);
+        const KiviMeta meta = make_meta(p, u);
+        {
+          const uint32_t s = nv % 2, ph = (nv / 2) & 1;
+          ++nv;
+          if (!mbar_wait(smem_u32(&sm.qv_empty[s]), ph ^ 1, p.err)) break;
+          sm.meta[s] = meta;  // published by the arrive below (release)
+          mbar_arrive_expect_tx(smem_u32(&sm.qv_full[s]), kQBytes);
+          bulk_load(smem_u32(sm.q[s]), p.q + u * kGroupHeads * kHeadDim, kQBytes, smem_u32(&sm.qv_full[s]));
+        }
+        // Quantized batches first when they all fit in the Q ring (their
+        // dequantization then overlaps the residual tiles).  Otherwise the
+        // residual tiles go first: the MMA warps consume a piece's residual
+        // tiles before its groups, so a producer stuck on a full Q ring must
+        // not hold back residual tiles they wait for.
+        int live_q = 0;
+        for (int64_t t = pc.t_begin; t < pc.t_end; ++t)
+          if (t < p.n_qb && item_live(p, meta, static_cast<int>(t))) ++live_q;
+        const bool q_first = live_q <= kQStages;
+        for (int pass = 0; pass < 2 && ok; ++pass) {
+          for (int64_t t = pc.t_begin; t < pc.t_end; ++t) {
+            const int itm = static_cast<int>(t);
+            const bool is_q = itm < p.n_qb;
+            if (is_q != ((pass == 0) == q_first) || !item_live(p, meta, itm)) continue;
+            if (is_q) {
+              const uint32_t s = nq % kQStages, ph = (nq / kQStages) & 1;
+              ++nq;
+              if (!mbar_wait(smem_u32(&sm.q_empty[s]), ph ^ 1, p.err)) { ok = false; break; }
+              const uint32_t fb = smem_u32(&sm.q_full[s]);
+              const uint32_t sd = smem_u32(sm.qb[s]);
+              sm.qhdr[s].meta = meta;
+              sm.qhdr[s].item = itm;
+              sm.qhdr[s].end = 0;
+              const int b = itm;
+              const bool has_sink = (b == 0);
+              const int p0 = b == 0 ? 0 : kBatchGroups * b - 1;
+              const int p1 = min(p.n_groups, kBatchGroups * b + kBatchGroups - 1);
+              const int so = p0 + 1 - kBatchGroups * b;  // batch slot of group p0
+              const uint32_t ng = p1 > p0 ? p1 - p0 : 0;
+              mbar_arrive_expect_tx(fb, (has_sink ? 3072u : 0u) + ng * 3072u);
+              if (has_sink) {
+                bulk_load(sd + kOffKP, p.ks_p + u * 1024, 1024, fb);
+                bulk_load(sd + kOffKS, p.ks_s + u * 128, 256, fb);
+                bulk_load(sd + kOffKZ, p.ks_z + u * 128, 256, fb);
+                bulk_load(sd + kOffVP, p.vs_p + u * 1024, 1024, fb);
+                bulk_load(sd + kOffVS, p.vs_s + u * 128, 256, fb);
+                bulk_load(sd + kOffVZ, p.vs_z + u * 128, 256, fb);
+              }
+              if (ng) {
+                const int64_t gbase = u * p.n_groups + p0;
+                bulk_load(sd + kOffKP + so * 1024, p.kw_p + gbase * 1024, ng * 1024, fb);
+                bulk_load(sd + kOffKS + so * 256, p.kw_s + gbase * 128, ng * 256, fb);
+                bulk_load(sd + kOffKZ + so * 256, p.kw_z + gbase * 128, ng * 256, fb);
+                bulk_load(sd + kOffVP + so * 1024, p.vw_p + gbase * 1024, ng * 1024, fb);
+                bulk_load(sd + kOffVS + so * 256, p.vw_s + gbase * 128, ng * 256, fb);
+                bulk_load(sd + kOffVZ + so * 256, p.vw_z + gbase * 128, ng * 256, fb);
+              }
+            } else {
+              const uint32_t s = nf % kFStages, ph = (nf / kFStages) & 1;
+              ++nf;
+              if (!mbar_wait(smem_u32(&sm.f_empty[s]), ph ^ 1, p.err)) { ok = false; break; }
+              const uint32_t fb = smem_u32(&sm.f_full[s]);
+              const uint32_t sd = smem_u32(sm.f[s]);
+              mbar_arrive_expect_tx(fb, kFStageBytes);
+              const int row = (itm - p.n_qb) * kTile;
+              const int uu = static_cast<int>(u);
+              tma_load_3d(sd, &tmK, fb, 0, row, uu);
+              tma_load_3d(sd + kRegionBytes, &tmK, fb, 64, row, uu);
+              tma_load_3d(sd + kTileBytes, &tmV, fb, 0, row, uu);
+              tma_load_3d(sd + kTileBytes + kRegionBytes, &tmV, fb, 64, row, uu);
             }
-            if (ng) {
-              const int64_t gbase = u * p.n_groups + p0;
-              bulk_load(sd + kOffKP + so * 1024, p.kw_p + gbase * 1024, ng * 1024, fb);
-              bulk_load(sd + kOffKS + so * 256, p.kw_s + gbase * 128, ng * 256, fb);
-              bulk_load(sd + kOffKZ + so * 256, p.kw_z + gbase * 128, ng * 256, fb);
-              bulk_load(sd + kOffVP + so * 1024, p.vw_p + gbase * 1024, ng * 1024, fb);
-              bulk_load(sd + kOffVS + so * 256, p.vw_s + gbase * 128, ng * 256, fb);
-              bulk_load(sd + kOffVZ + so * 256, p.vw_z + gbase * 128, ng * 256, fb);
-            }
-          } else {
-            mbar_arrive_expect_tx(fb, kStageBytes);
-            const int row = (itm - p.n_qb) * kTile;
-            const int uu = static_cast<int>(u);
-            tma_load_3d(sd, &tmK, fb, 0, row, uu);
-            tma_load_3d(sd + kRegionBytes, &tmK, fb, 64, row, uu);
-            tma_load_3d(sd + kTileBytes, &tmV, fb, 0, row, uu);
-            tma_load_3d(sd + kTileBytes + kRegionBytes, &tmV, fb, 64, row, uu);
           }
+        }
+      }
+      if (ok) {
+        // sentinel for the dequantizers
+        const uint32_t s = nq % kQStages, ph = (nq / kQStages) & 1;
+        if (mbar_wait(smem_u32(&sm.q_empty[s]), ph ^ 1, p.err)) {
+          sm.qhdr[s].end = 1;
+          mbar_arrive(smem_u32(&sm.q_full[s]));
         }
       }
     }
     return;
   }
 
-  // ------------------------------------------------------------ consumers
-  const int grp = warp / kGroupWarps, wq = warp % kGroupWarps;
+  if (warp >= kMmaWarps) {
+    // ------------------------------------------------------- dequantizers
+    const int dw = warp - kMmaWarps;
+    uint32_t nq = 0, ng = 0;  // Q stages consumed; live groups seen (all dequant warps count alike)
+    for (;;) {
+      const uint32_t s = nq % kQStages, ph = (nq / kQStages) & 1;
+      ++nq;
+      if (!mbar_wait(smem_u32(&sm.q_full[s]), ph, p.err)) return;
+      const QHeader hdr = sm.qhdr[s];
+      if (hdr.end) return;
+      const uint32_t qs = smem_u32(sm.qb[s]);
+      for (int slot = 0; slot < kBatchGroups; ++slot) {
+        const uint32_t mask = group_mask(p, hdr.meta, hdr.item, slot);
+        if (!mask) continue;
+        const uint32_t n = ng++;
+        if (static_cast<int>(n % kDqWarps) != dw) continue;
+        const uint32_t ds = dw, dph = (n / kDqWarps) & 1;
+        if (!mbar_wait(smem_u32(&sm.dq_empty[ds]), dph ^ 1, p.err)) return;
+        dequant_group(qs, slot, smem_u32(sm.dq[ds]), mask, lane);
+        if (lane == 0) sm.dq_mask[ds] = mask;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sm.dq_full[ds]));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sm.q_empty[s]));
+    }
+  }
+
+  // -------------------------------------------------------------- MMA warps
+  // A timed-out wait sets `aborted`: the warp then stops waiting (the error
+  // word is already set) but keeps its schedule of named barriers.
   const int g = lane >> 2;
-  int qs = 0;
-  uint32_t qphase = 0, k = 0;
+  uint32_t nv = 0, nf = 0, ng = 0, job = 0;
   bool aborted = false;
   WarpAttn st;
-  const uint32_t scr_k = smem_u32(sm.scratch[warp][0]);
-  const uint32_t scr_v = smem_u32(sm.scratch[warp][1]);
   PieceIter it(p);
   Piece pc;
   while (it.next(p, pc)) {
-    if (!aborted && !mbar_wait(smem_u32(&sm.q_full[qs]), qphase, p.err)) aborted = true;
-    // Q fragments are reloaded from the slot for every 16-token job (so they
-    // are not live across the dequantization); the slot is released after
-    // the piece's last job.
-    const uint32_t qaddr = smem_u32(sm.q[qs]);
-    const int qslot = qs;
-    const KiviMeta meta = sm.meta[qs];
-    if (++qs == 2) { qs = 0; qphase ^= 1; }
+    const uint32_t vs = nv % 2, vph = (nv / 2) & 1;
+    ++nv;
+    if (!aborted && !mbar_wait(smem_u32(&sm.qv_full[vs]), vph, p.err)) aborted = true;
+    st.load_q(smem_u32(sm.q[vs]), lane);
+    const KiviMeta meta = sm.meta[vs];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&sm.qv_empty[vs]));
     st.reset();
+    // residual tiles first, then the dequantized groups (the producer issued
+    // the quantized batches first so their dequantization overlaps)
     for (int64_t t = pc.t_begin; t < pc.t_end; ++t) {
       const int itm = static_cast<int>(t);
-      if (!item_live(p, meta, itm)) continue;
-      const uint32_t kk = k++;
-      if ((kk % kGroups) != static_cast<uint32_t>(grp)) continue;
-      const uint32_t stage = kk % kStages, phase = (kk / kStages) & 1;
-      if (!aborted && !mbar_wait(smem_u32(&sm.full[stage]), phase, p.err)) aborted = true;
-      const uint32_t sd = smem_u32(sm.stage[stage]);
-      const bool is_q = itm < p.n_qb;
-      // Jobs of 16 tokens for this warp: a Q-batch has 16 half-groups (this
-      // warp takes every 4th, dequantized into its scratch tile); an F-tile
-      // has one (rows 16wq.. of the TMA tile).  One engine call site serves
-      // both so the kernel stays within its register budget.
-      for (int mt = wq; mt < (is_q ? 2 * kBatchGroups : wq + 1); mt += kGroupWarps) {
-        uint32_t kb, vb, rb;
-        int row0;
-        bool v_lo, v_hi;
-        if (is_q) {
-          const int slot = mt >> 1, hf = mt & 1;
-          // validity of the 16 tokens of this half (bit t = token 16hf + t)
-          uint32_t vm = 0;
-          if (lane < 16) vm = q_token_valid(p, meta, itm, slot, 16 * hf + lane) ? 1u : 0u;
-          vm = __ballot_sync(0xffffffffu, vm != 0) & 0xffffu;
-          if (vm == 0) continue;
-          dequant_k16(sd, scr_k, slot, hf, lane, vm);
-          dequant_v16(sd, scr_v, slot, hf, lane, vm);
-          __syncwarp();
-          kb = scr_k;
-          vb = scr_v;
-          rb = kScratchRegion;
-          row0 = 0;
-          v_lo = (vm >> g) & 1u;
-          v_hi = (vm >> (g + 8)) & 1u;
-        } else {
-          const int r0 = (itm - p.n_qb) * kTile + 16 * wq;
-          v_lo = res_slot_valid(p, meta, r0 + g);
-          v_hi = res_slot_valid(p, meta, r0 + g + 8);
-          kb = sd;
-          vb = sd + kTileBytes;
-          rb = kRegionBytes;
-          row0 = 16 * wq;
-          zero_invalid_v_rows(vb, rb, row0, v_lo, v_hi, lane);
-        }
-        st.load_q(qaddr, lane);
-        st.consume16(kb, vb, rb, row0, v_lo, v_hi, p.scale_log2, lane);
-        __syncwarp();  // scratch is rewritten by the next job
+      if (itm < p.n_qb || !item_live(p, meta, itm)) continue;
+      const uint32_t s = nf % kFStages, ph = (nf / kFStages) & 1;
+      ++nf;
+      if (!aborted && !mbar_wait(smem_u32(&sm.f_full[s]), ph, p.err)) aborted = true;
+      const uint32_t sd = smem_u32(sm.f[s]);
+      const int r0 = (itm - p.n_qb) * kTile + 16 * warp;
+      const bool v_lo = res_slot_valid(p, meta, r0 + g);
+      const bool v_hi = res_slot_valid(p, meta, r0 + g + 8);
+      if (__any_sync(0xffffffffu, v_lo || v_hi)) {
+        zero_invalid_v_rows(sd + kTileBytes, kRegionBytes, 16 * warp, v_lo, v_hi, lane);
+        st.consume16(sd, sd + kTileBytes, kRegionBytes, 16 * warp, v_lo, v_hi, p.scale_log2, lane);
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sm.empty[stage]));
+      if (lane == 0) mbar_arrive(smem_u32(&sm.f_empty[s]));
+    }
+    for (int64_t t = pc.t_begin; t < pc.t_end; ++t) {
+      const int itm = static_cast<int>(t);
+      if (itm >= p.n_qb || !item_live(p, meta, itm)) continue;
+      for (int slot = 0; slot < kBatchGroups; ++slot) {
+        if (!group_mask(p, meta, itm, slot)) continue;
+        const uint32_t n = ng++;
+        const uint32_t ds = n % kDqWarps, dph = (n / kDqWarps) & 1;  // group n is in its dequantizer's slot
+        if (!aborted && !mbar_wait(smem_u32(&sm.dq_full[ds]), dph, p.err)) aborted = true;
+        const uint32_t mask = sm.dq_mask[ds];
+        const uint32_t dbase = smem_u32(sm.dq[ds]);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const uint32_t hm = (mask >> (16 * hf)) & 0xffffu;
+          if (!hm) continue;
+          if ((job++ % kMmaWarps) != static_cast<uint32_t>(warp)) continue;
+          st.consume16(dbase, dbase + kDqTile, kDqRegion, 16 * hf, (hm >> g) & 1u, (hm >> (g + 8)) & 1u,
+                       p.scale_log2, lane);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sm.dq_empty[ds]));
+      }
     }
 
-    __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(&sm.q_empty[qslot]));
-
-    // ---- epilogue (as in the fp16 kernel)
-    if (grp == 1) warp_xfer_out(st, sm.ep, wq, lane);
-    consumer_sync();
-    if (grp == 0) warp_xfer_in(st, sm.ep, wq, lane);
-    consumer_sync();
-    if (grp == 0) warp_publish(st, sm.ep, wq, lane);
-    consumer_sync();
-    const int ct = threadIdx.x;
-    const int hh = ct >> 5, d0 = (ct & 31) * 4;
-    float o[4], lse;
-    merge_warps(sm.ep, hh, d0, o, lse);
+    // ---- epilogue: merge the 4 MMA warps, write the output or a partial
+    warp_publish(st, sm.ep, warp, lane);
+    mma_warps_sync();
+    const int ct = threadIdx.x;  // 0..127
+    const int hh = ct >> 4, d0 = (ct & 15) * 8;
+    float o[8], lse;
+    {
+      float o4[4];
+      merge_warps(sm.ep, hh, d0, o4, lse);
+      for (int i = 0; i < 4; ++i) o[i] = o4[i];
+      merge_warps(sm.ep, hh, d0 + 4, o4, lse);
+      for (int i = 0; i < 4; ++i) o[4 + i] = o4[i];
+    }
     __half* out = p.o + pc.unit * kGroupHeads * kHeadDim;
     if (pc.n_pieces == 1) {
-      store_half4(out + hh * kHeadDim + d0, o);
+      const float a[4] = {o[0], o[1], o[2], o[3]}, b[4] = {o[4], o[5], o[6], o[7]};
+      store_half4(out + hh * kHeadDim + d0, a);
+      store_half4(out + hh * kHeadDim + d0 + 4, b);
     } else {
       const int64_t pidx = pc.unit * p.max_pieces + pc.slot;
       float* po = p.part_o + (pidx * kGroupHeads + hh) * kHeadDim + d0;
-      *reinterpret_cast<float4*>(po) = make_float4(o[0], o[1], o[2], o[3]);
-      if ((ct & 31) == 0) p.part_lse[pidx * kGroupHeads + hh] = lse;
+      reinterpret_cast<float4*>(po)[0] = make_float4(o[0], o[1], o[2], o[3]);
+      reinterpret_cast<float4*>(po)[1] = make_float4(o[4], o[5], o[6], o[7]);
+      if ((ct & 15) == 0) p.part_lse[pidx * kGroupHeads + hh] = lse;
       __threadfence();
-      consumer_sync();
+      mma_warps_sync();
       if (ct == 0) sm.ep.ticket = atomicAdd(p.counters + pc.unit, 1);
-      consumer_sync();
+      mma_warps_sync();
       if (sm.ep.ticket == pc.n_pieces - 1) {
         __threadfence();
         const int64_t base = pc.unit * p.max_pieces;
         combine_pieces(p.part_lse + base * kGroupHeads, p.part_o + base * kGroupHeads * kHeadDim, pc.n_pieces, out,
-                       warp, lane);
+                       warp * (kGroupHeads / kMmaWarps), kGroupHeads / kMmaWarps, lane);
         if (ct == 0) p.counters[pc.unit] = 0;
       }
     }
-    consumer_sync();
+    mma_warps_sync();
   }
 }
 
