@@ -37,14 +37,82 @@ struct WarpAttn {
       for (int c = 0; c < 4; ++c) acc[j][c] = 0.f;
   }
 
-  // Q^T B-fragments from an unswizzled [8 heads][128] fp16 smem block.
-  __device__ __forceinline__ void load_q(uint32_t qbase, int lane) {
+  // Q^T B-fragments from an unswizzled [8 heads][128] fp16 smem block whose
+  // rows are `row_bytes` apart.
+  __device__ __forceinline__ void load_q(uint32_t qbase, int lane, uint32_t row_bytes = 256) {
     const int mi = lane >> 3, head = lane & 7;
 #pragma unroll
     for (int ks = 0; ks < 8; ks += 2) {
       const int dim = 16 * (ks + (mi >> 1)) + (mi & 1) * 8;
-      ldmatrix_x4(qbase + head * 256 + dim * 2, qb[ks][0], qb[ks][1], qb[ks + 1][0], qb[ks + 1][1]);
+      ldmatrix_x4(qbase + head * row_bytes + dim * 2, qb[ks][0], qb[ks][1], qb[ks + 1][0], qb[ks + 1][1]);
     }
+  }
+
+  // Online-softmax step for N blocks of 16 rows: raw scores s[h][] of rows g /
+  // g+8 of block h for heads 2t / 2t+1 (g = lane / 4, t = lane % 4); rescales
+  // the running state once and returns each block's P^T B-fragments (pb[h][0]:
+  // rows 2t, 2t+1; pb[h][1]: rows 2t+8, 2t+9; column = head g).
+  template <int N>
+  __device__ __forceinline__ void softmax_rows(float (&s)[N][4], const bool (&valid_lo)[N], const bool (&valid_hi)[N],
+                                               float scale_log2, uint32_t (&pb)[N][2]) {
+    // scores in log2 units; masked rows -> -inf
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int h = 0; h < N; ++h) {
+      s[h][0] = valid_lo[h] ? s[h][0] * scale_log2 : -INFINITY;
+      s[h][1] = valid_lo[h] ? s[h][1] * scale_log2 : -INFINITY;
+      s[h][2] = valid_hi[h] ? s[h][2] * scale_log2 : -INFINITY;
+      s[h][3] = valid_hi[h] ? s[h][3] * scale_log2 : -INFINITY;
+      mx0 = fmaxf(mx0, fmaxf(s[h][0], s[h][2]));
+      mx1 = fmaxf(mx1, fmaxf(s[h][1], s[h][3]));
+    }
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float mn0 = fmaxf(m[0], mx0);
+    const float mn1 = fmaxf(m[1], mx1);
+    // reference point: 0 while nothing valid has been seen (avoids inf - inf)
+    const float b0 = (mn0 == -INFINITY) ? 0.f : mn0;
+    const float b1 = (mn1 == -INFINITY) ? 0.f : mn1;
+    const float al0 = fast_exp2(m[0] - b0);
+    const float al1 = fast_exp2(m[1] - b1);
+    float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+    for (int h = 0; h < N; ++h) {
+      const float p0 = fast_exp2(s[h][0] - b0);
+      const float p1 = fast_exp2(s[h][1] - b1);
+      const float p2 = fast_exp2(s[h][2] - b0);
+      const float p3 = fast_exp2(s[h][3] - b1);
+      sum0 += p0 + p2;
+      sum1 += p1 + p3;
+      pb[h][0] = movmatrix_trans(pack_half2(p0, p1));  // P[tok 2t,2t+1][head g]
+      pb[h][1] = movmatrix_trans(pack_half2(p2, p3));  // P[tok 2t+8,2t+9][head g]
+    }
+    l[0] = l[0] * al0 + sum0;
+    l[1] = l[1] * al1 + sum1;
+    m[0] = mn0;
+    m[1] = mn1;
+    if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {  // skipped while no running max moves
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        acc[j][0] *= al0;
+        acc[j][1] *= al1;
+        acc[j][2] *= al0;
+        acc[j][3] *= al1;
+      }
+    }
+  }
+
+  __device__ __forceinline__ void softmax16(float (&s)[4], bool valid_lo, bool valid_hi, float scale_log2,
+                                            uint32_t& pb0, uint32_t& pb1) {
+    float sh[1][4] = {{s[0], s[1], s[2], s[3]}};
+    const bool vl[1] = {valid_lo}, vh[1] = {valid_hi};
+    uint32_t pb[1][2];
+    softmax_rows<1>(sh, vl, vh, scale_log2, pb);
+    pb0 = pb[0][0];
+    pb1 = pb[0][1];
   }
 
   // Consume tokens [row0, row0+16) of a swizzled tile whose regions are
@@ -71,42 +139,8 @@ struct WarpAttn {
 #pragma unroll
       for (int c = 0; c < 4; ++c) s[c] += s2[c];
     }
-    // scores in log2 units; masked rows -> -inf
-    s[0] = valid_lo ? s[0] * scale_log2 : -INFINITY;
-    s[1] = valid_lo ? s[1] * scale_log2 : -INFINITY;
-    s[2] = valid_hi ? s[2] * scale_log2 : -INFINITY;
-    s[3] = valid_hi ? s[3] * scale_log2 : -INFINITY;
-    float mx0 = fmaxf(s[0], s[2]);
-    float mx1 = fmaxf(s[1], s[3]);
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-    }
-    const float mn0 = fmaxf(m[0], mx0);
-    const float mn1 = fmaxf(m[1], mx1);
-    // reference point: 0 while nothing valid has been seen (avoids inf - inf)
-    const float b0 = (mn0 == -INFINITY) ? 0.f : mn0;
-    const float b1 = (mn1 == -INFINITY) ? 0.f : mn1;
-    const float al0 = fast_exp2(m[0] - b0);
-    const float al1 = fast_exp2(m[1] - b1);
-    const float p0 = fast_exp2(s[0] - b0);
-    const float p1 = fast_exp2(s[1] - b1);
-    const float p2 = fast_exp2(s[2] - b0);
-    const float p3 = fast_exp2(s[3] - b1);
-    l[0] = l[0] * al0 + (p0 + p2);
-    l[1] = l[1] * al1 + (p1 + p3);
-    m[0] = mn0;
-    m[1] = mn1;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      acc[j][0] *= al0;
-      acc[j][1] *= al1;
-      acc[j][2] *= al0;
-      acc[j][3] *= al1;
-    }
-    const uint32_t pb0 = movmatrix_trans(pack_half2(p0, p1));  // P[tok 2t,2t+1][head g]
-    const uint32_t pb1 = movmatrix_trans(pack_half2(p2, p3));  // P[tok 2t+8,2t+9][head g]
+    uint32_t pb0, pb1;
+    softmax16(s, valid_lo, valid_hi, scale_log2, pb0, pb1);
     {
       const uint32_t mi = lane >> 3;
       const uint32_t row = row0 + (mi >> 1) * 8 + (lane & 7);

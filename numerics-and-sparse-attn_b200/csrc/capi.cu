@@ -1,5 +1,6 @@
 // Status plumbing, device error word and tensor-map encoding for the C ABI.
 #include <cstdarg>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -80,6 +81,14 @@ EncodeFn encode_fn() {
   return fn;
 }
 }  // namespace
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("NSA_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, const void* base,
                  const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,

@@ -165,6 +165,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     fp16_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                        const Params p) {
   extern __shared__ uint8_t smem_raw[];
+  grid_launch_dependents();
+  grid_dependency_wait();  // the cache and q may come from the previous kernel of the stream
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -393,8 +395,8 @@ int launch(Params& p, const Split& s, const void* k, const void* v, int64_t cap,
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     attr_set[dev] = true;
   }
-  fp16_decode_kernel<<<s.n_ctas, kThreads, kSmemBytes, stream>>>(mk, mv, p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_kernel(fp16_decode_kernel, dim3(s.n_ctas), dim3(kThreads), kSmemBytes, stream, mk, mv, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "fp16_decode_kernel launch");
   return NSA_OK;
 }

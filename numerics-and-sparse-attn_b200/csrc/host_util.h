@@ -9,6 +9,7 @@
 
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "nsa_b200.h"
 
@@ -38,6 +39,31 @@ int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, con
                  CUtensorMapSwizzle swizzle);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Whether launches use programmatic dependent launch (default on; NSA_PDL=0
+// turns it off).  Every kernel of this library waits (griddepcontrol.wait)
+// before it reads or writes global memory that an earlier kernel of the
+// stream may use, so the attribute only lets its prologue overlap the tail of
+// the previous kernel.
+bool pdl_enabled();
+
+// Launch `kernel` on `stream` with the programmatic-stream-serialization
+// attribute when pdl_enabled().
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace nsa
 

@@ -2,28 +2,42 @@
 // :316-581) over either the reference's 14-tensor layout or the streaming
 // ring layout of nsa_kivi_stream_cache.
 //
-// Per (batch, kv_head) unit the work is a fixed list of items:
-//   F-tiles    64 slots of the fp16 residual (ring), staged by TMA with the
-//              128-byte swizzle (F ring, 3 x 32 KiB);
-//   Q-batches  up to 6 quantized 32-token groups (slot 0 of batch 0 is the
-//              padded sink group, then window groups in physical order),
-//              staged with 1-D bulk copies, 3 KiB per group (Q ring, 2 x 18 KiB).
-// Items holding no attended token are skipped by every role alike (all derive
-// it from the same per-unit metadata).
+// Work: one CTA per piece, two CTAs per SM.  A piece is one unit (batch row,
+// KV head) -- or, when there are fewer units than CTA slots, a contiguous part
+// of the unit's items, merged by the split-K combine.  With every unit resident
+// at once, all of a launch's loads are in flight from the start.  Per unit the
+// items, in issue and consumption order, are: Q-batch 0, the F-tiles, the
+// other Q-batches, where
+//   Q-batch    up to 5 quantized 32-token groups (slot 0 of batch 0 is the
+//              padded sink group, then window groups in physical order), staged
+//              raw -- codes, scales, zero points -- by 1-D bulk copies, 3 KiB
+//              per group (Q ring, 2 x 15 KiB);
+//   F-tile     80 slots of the fp16 residual ring, K and V each staged by one
+//              TMA box (both 64-dim halves, 128-byte swizzle) (F ring, 2 x 40 KiB).
+// Batch 0 carries most of the arithmetic, so it is loaded and consumed first
+// and its dequantization overlaps the residual's transfer.  Every TMA request
+// costs a fixed issue time (about 40 ns on B200) whatever its size, so loads
+// are few and large, and those that do not depend on the unit's length (query,
+// batch 0, residual) are issued before that length is read.  Q-batches after
+// the first that hold no attended token are skipped by every warp alike.
 //
-// Warp roles (warp specialization):
-//   warp 8      producer: issues the loads of both rings;
-//   warps 4-7   dequantizers: each turns whole quantized groups (round-robin)
-//               into swizzled fp16 K/V tiles in its own DQ slot, writing
-//               zeros for unattended V rows;
-//   warps 0-3   MMA warps: consume fp16 tiles -- residual tiles straight from
-//               the F ring (warp w takes rows 16w..16w+15) and dequantized
-//               groups from the DQ ring (16-token halves round-robin) -- with
-//               the shared mma.sync engine, then run the epilogue.
-// Dequantization thus overlaps the tensor-core work and the loads instead of
-// sitting in front of them.  Every ring has all of its consumers wait on every
-// phase, as parity waits require.  Scheduling (whole units per CTA, or
-// stream-K with the in-launch combine) is the fp16 kernel's.
+// Warp 4 issues the loads; warps 0-3 consume, taking jobs (a quantized group,
+// or 16 rows of an F-tile) by a static cost-balanced assignment that every warp
+// computes alike.  A quantized group is dequantized in
+// registers straight into mma.sync fragments, with no shared-memory round trip:
+//   K  S^T = (C - Z) (s*Q)^T: the per-channel scale s is folded into the query
+//      once per group; C (2-bit codes as exact fp16 integers, made with the
+//      1024-style magic-number trick) is the A operand; the zero-point term
+//      Z (s*Q)^T is one mma chain whose A rows all equal z, computed once per
+//      group and used as the initial score.  The mma's k index is permuted so
+//      that each lane's codes are whole bytes of one packed row (the query
+//      fragments are permuted to match), and the mma's rows are a fixed
+//      permutation of the group's tokens so that a lane's two rows share a byte.
+//   V  O^T += (C - Z)^T (P*s)^T per 32-channel group: c - z is exact for the
+//      integer zero points, and the per-token scale is folded into the P
+//      fragment of each channel group (one rounding, as in an fp16
+//      dequantization of the cache).
+// F-tiles go through the shared fp16 engine (consume16).
 #include <cstddef>
 #include <cstdlib>
 
@@ -33,29 +47,24 @@
 namespace nsa {
 namespace {
 
-constexpr int kMmaWarps = 4;
-constexpr int kDqWarps = 4;
-constexpr int kProducerWarp = kMmaWarps + kDqWarps;
-constexpr int kThreads = (kProducerWarp + 1) * 32;
-constexpr int kFStages = 3;
+constexpr int kCWarps = 4;                 // consumer warps
+constexpr int kProducerWarp = kCWarps;
+constexpr int kThreads = (kCWarps + 1) * 32;
+constexpr int kCtasPerSm = 2;
+constexpr int kFRows = 80;                 // residual slots per F-tile
+constexpr uint32_t kFRegion = kFRows * 128;  // 80 rows x 64 dims fp16
+constexpr uint32_t kFTile = 2 * kFRegion;    // K (or V) of one F-tile: one TMA box
+constexpr uint32_t kFStageBytes = 2 * kFTile;  // 40 KiB
+constexpr int kFStages = 2;
 constexpr int kQStages = 2;
-// One DQ slot per dequantizer: a slot then alternates strictly between its
-// own warp's production and the MMA warps' release, so a parity wait on it can
-// never be two phases behind (a slot shared by independent producers could).
-constexpr int kDqSlots = kDqWarps;
-constexpr uint32_t kRegionBytes = kTile * 128;
-constexpr uint32_t kTileBytes = 2 * kRegionBytes;
-constexpr uint32_t kFStageBytes = 2 * kTileBytes;  // 32 KiB: K + V of 64 slots
+constexpr int kBatchGroups = 5;            // quantized groups per Q-batch
 constexpr uint32_t kQBytes = kGroupHeads * kHeadDim * 2;
-constexpr int kBatchGroups = 6;                    // quantized groups per Q-batch
+constexpr int kQPadStride = kHeadDim + 8;  // 272-byte rows: 8 rows of an ldmatrix hit distinct banks
 // Q-batch stage layout (byte offsets); one slot per group
 constexpr uint32_t kOffKP = 0, kOffKS = kBatchGroups * 1024, kOffKZ = kOffKS + kBatchGroups * 256,
                    kOffVP = kOffKZ + kBatchGroups * 256, kOffVS = kOffVP + kBatchGroups * 1024,
                    kOffVZ = kOffVS + kBatchGroups * 256;
 constexpr uint32_t kQStageBytes = kOffVZ + kBatchGroups * 256;  // 3 KiB per group
-constexpr uint32_t kDqRegion = 32 * 128;           // 32 rows x 64 dims fp16
-constexpr uint32_t kDqTile = 2 * kDqRegion;        // K (or V) of one group
-constexpr uint32_t kDqSlotBytes = 2 * kDqTile;     // K + V, 16 KiB
 
 struct KiviMeta {
   int32_t n_sink;    // attended sink tokens
@@ -68,32 +77,25 @@ struct KiviMeta {
   int32_t pad;
 };
 
-struct QHeader {  // written by the producer into each Q-ring stage
-  KiviMeta meta;
-  int32_t item;  // Q-batch index within its unit
-  int32_t end;   // 1: no more work (sentinel for the dequantizers)
-};
-
 struct Smem {
-  // copy destinations first: every one stays 16-byte (TMA tiles: 1024-byte) aligned
-  uint8_t f[kFStages][kFStageBytes];  // 1024-aligned
-  uint8_t dq[kDqSlots][kDqSlotBytes];
+  union {
+    uint8_t f[kFStages][kFStageBytes];  // 1024-aligned TMA tile destinations
+    EpilogueSmem ep;                    // reused once every item has been consumed
+  };
   uint8_t qb[kQStages][kQStageBytes];
-  uint8_t q[2][kQBytes];
-  EpilogueSmem ep;
-  QHeader qhdr[kQStages];
-  KiviMeta meta[2];
-  uint32_t dq_mask[kDqSlots];         // attended tokens of the group in each DQ slot
+  __half qpad[kGroupHeads][kQPadStride];  // the unit's query, rows padded: conflict-free fragment loads
   uint64_t f_full[kFStages], f_empty[kFStages];
   uint64_t q_full[kQStages], q_empty[kQStages];
-  uint64_t dq_full[kDqSlots], dq_empty[kDqSlots];
-  uint64_t qv_full[2], qv_empty[2];
 };
 
-static_assert(offsetof(Smem, f) % 1024 == 0 && kFStageBytes % 1024 == 0, "TMA tile destinations");
+static_assert(offsetof(Smem, f) == 0 && kFStageBytes % 1024 == 0 && kFRegion % 1024 == 0, "TMA tile destinations");
 static_assert(offsetof(Smem, qb) % 16 == 0 && kQStageBytes % 16 == 0, "bulk-copy destinations");
-static_assert(offsetof(Smem, q) % 16 == 0 && kQBytes % 16 == 0, "bulk-copy destinations");
-static_assert(offsetof(Smem, dq) % 128 == 0, "dequantized tiles");
+static_assert(offsetof(Smem, qpad) % 16 == 0 && (kQPadStride * 2) % 16 == 0, "16-byte stores");
+static_assert(sizeof(EpilogueSmem) <= sizeof(uint8_t[kFStages][kFStageBytes]), "epilogue alias");
+// The dynamic shared-memory window of a CTA starts 1024-byte aligned on sm_100
+// (the kernel checks it); 1 KiB per CTA is reserved by the system.
+constexpr size_t kSmemBytes = sizeof(Smem);
+static_assert(kCtasPerSm * (kSmemBytes + 1024) <= 228 * 1024, "two CTAs per SM");
 
 struct KParams {
   const __half* q;
@@ -104,12 +106,8 @@ struct KParams {
   int64_t seq_len;
   const int64_t* unit_lens;
   int window, sink, residual, n_groups, res_cap;
-  int n_qb, n_ft;
-  int64_t tiles_per_unit;  // items per unit
-  int64_t total_tiles;
-  int n_ctas;
-  int unit_aligned;
-  int max_pieces;
+  int n_qb, n_ft, items;  // items per unit: Q-batch 0, n_ft F-tiles, Q-batches 1 .. n_qb-1
+  int ppu;                // pieces (CTAs) per unit
   float scale_log2;
   const uint8_t* ks_p;
   const __half* ks_s;
@@ -163,22 +161,28 @@ __device__ __forceinline__ KiviMeta make_meta(const KParams& p, int64_t unit) {
     m.grp_head = NG > 0 ? static_cast<int32_t>((F - m.n_grp) % NG) : 0;
     m.tok_skip = clampi(first - S - 32 * (F - m.n_grp), 0, 32 * int64_t(m.n_grp));
   }
+  m.pad = 0;
   return m;
 }
 
-// Distance of window-group slot p from the oldest live group (>= n_grp: dead).
+// Distance of window-group slot gp from the oldest live group (>= n_grp: dead).
 __device__ __forceinline__ int grp_age(const KParams& p, const KiviMeta& m, int gp) {
   int d = gp - m.grp_head;
   if (d < 0) d += p.n_groups;
   return d;
 }
 
-__device__ __forceinline__ bool q_slot_live(const KParams& p, const KiviMeta& m, int b, int slot) {
+// Attended-token mask (bit j = token j) of batch slot `slot` of Q-batch `b`.
+__device__ __forceinline__ uint32_t group_mask(const KParams& p, const KiviMeta& m, int b, int slot) {
   const int v = kBatchGroups * b + slot;
-  if (v == 0) return m.n_sink > 0;
-  if (v > p.n_groups) return false;
+  if (v == 0) return m.n_sink >= 32 ? 0xffffffffu : ((1u << m.n_sink) - 1u);
+  if (v > p.n_groups) return 0;
   const int age = grp_age(p, m, v - 1);
-  return age < m.n_grp && 32 * age + 31 >= m.tok_skip;
+  if (age >= m.n_grp) return 0;
+  const int first = m.tok_skip - 32 * age;  // tokens below this one are not attended
+  if (first <= 0) return 0xffffffffu;
+  if (first >= 32) return 0;
+  return ~((1u << first) - 1u);
 }
 
 __device__ __forceinline__ bool res_slot_valid(const KParams& p, const KiviMeta& m, int r) {
@@ -188,159 +192,219 @@ __device__ __forceinline__ bool res_slot_valid(const KParams& p, const KiviMeta&
   return d >= m.res_skip && d < m.n_res;
 }
 
-// Whether item `it` of a unit holds any attended token.
-__device__ __forceinline__ bool item_live(const KParams& p, const KiviMeta& m, int it) {
-  if (it < p.n_qb) {
-    for (int s = 0; s < kBatchGroups; ++s)
-      if (q_slot_live(p, m, it, s)) return true;
-    return false;
-  }
-  // attended residual slots form the ring interval [a, a + len) mod C
-  const int r0 = (it - p.n_qb) * kTile, r1 = min(r0 + kTile, p.res_cap);
-  const int len = m.n_res - m.res_skip;
-  if (len <= 0 || r1 <= r0) return false;
-  int a = m.res_head + m.res_skip;
-  if (a >= p.res_cap) a -= p.res_cap;
-  const int e = a + len;
-  if (max(a, r0) < min(min(e, p.res_cap), r1)) return true;
-  return e > p.res_cap && r0 < e - p.res_cap;
+// Whether Q-batch b holds any attended token.  Batch 0 counts as live always:
+// its sink group is loaded before the unit's length is known.
+__device__ __forceinline__ bool batch_live(const KParams& p, const KiviMeta& m, int b) {
+  if (b == 0) return true;
+  for (int s = 0; s < kBatchGroups; ++s)
+    if (group_mask(p, m, b, s)) return true;
+  return false;
 }
 
-// CTA owning global item X under the even split of `total` items over `ctas`.
-__device__ __forceinline__ int64_t owner_cta(int64_t X, int64_t total, int64_t ctas) {
-  return ((X + 1) * ctas + total - 1) / total - 1;
-}
-
-struct Piece {
-  int64_t unit, t_begin, t_end;
-  int slot, n_pieces;
-};
-
-struct PieceIter {
-  int64_t X, X1;
-  __device__ __forceinline__ PieceIter(const KParams& p) {
-    const int64_t c = blockIdx.x;
-    if (p.unit_aligned) {
-      X = (c * p.n_units / p.n_ctas) * p.tiles_per_unit;
-      X1 = ((c + 1) * p.n_units / p.n_ctas) * p.tiles_per_unit;
-    } else {
-      X = c * p.total_tiles / p.n_ctas;
-      X1 = (c + 1) * p.total_tiles / p.n_ctas;
-    }
+// Static job assignment: each job goes to the consumer warp with the least
+// estimated work so far (all warps run the same sequence, so they agree).
+struct JobSched {
+  int cost[kCWarps];
+  __device__ __forceinline__ JobSched() {
+#pragma unroll
+    for (int w = 0; w < kCWarps; ++w) cost[w] = 0;
   }
-  __device__ __forceinline__ bool next(const KParams& p, Piece& pc) {
-    if (X >= X1) return false;
-    const int64_t tpu = p.tiles_per_unit;
-    pc.unit = X / tpu;
-    const int64_t ub = pc.unit * tpu, ue = ub + tpu;
-    const int64_t e = min(X1, ue);
-    pc.t_begin = X - ub;
-    pc.t_end = e - ub;
-    if (p.unit_aligned) {
-      pc.slot = 0;
-      pc.n_pieces = 1;
-    } else {
-      const int64_t c0 = owner_cta(ub, p.total_tiles, p.n_ctas);
-      const int64_t c1 = owner_cta(ue - 1, p.total_tiles, p.n_ctas);
-      pc.slot = static_cast<int>(blockIdx.x - c0);
-      pc.n_pieces = static_cast<int>(c1 - c0 + 1);
-    }
-    X = e;
-    return true;
+  __device__ __forceinline__ int take(int c) {
+    int best = 0, bc = cost[0];
+#pragma unroll
+    for (int w = 1; w < kCWarps; ++w)
+      if (cost[w] < bc) {
+        bc = cost[w];
+        best = w;
+      }
+#pragma unroll
+    for (int w = 0; w < kCWarps; ++w) cost[w] += (w == best) ? c : 0;  // static indexing: stays in registers
+    return best;
   }
 };
+constexpr int kCostF = 1;           // 16 fp16 residual rows
+constexpr int kCostGroup = 2;       // per quantized group (query scaling, zero-point term)
+constexpr int kCostGroupHalf = 3;   // per 16 attended-token half of a quantized group
 
-// ---------------------------------------------------------------- dequant
-// 2-bit codes -> fp16 via the 1024 + c exponent trick: (bits | 0x6400) is
-// the half 1024 + bits, exact for bits < 1024.
+// ---------------------------------------------------------------- registers
 __device__ __forceinline__ __half2 u32_as_h2(uint32_t x) { return *reinterpret_cast<__half2*>(&x); }
 __device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-
+__device__ __forceinline__ uint32_t hsub2u(uint32_t a, uint32_t b) {
+  return h2_as_u32(__hsub2(u32_as_h2(a), u32_as_h2(b)));
+}
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
+  return h2_as_u32(__hmul2(u32_as_h2(a), u32_as_h2(b)));
+}
+__device__ __forceinline__ uint32_t hadd2u(uint32_t a, uint32_t b) {
+  return h2_as_u32(__hadd2(u32_as_h2(a), u32_as_h2(b)));
+}
 __device__ __forceinline__ void lds128(uint32_t a, uint32_t& x, uint32_t& y, uint32_t& z, uint32_t& w) {
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(x), "=r"(y), "=r"(z), "=r"(w) : "r"(a));
 }
 __device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
   asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w));
 }
+__device__ __forceinline__ void lds64(uint32_t a, uint32_t& x, uint32_t& y) {
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(x), "=r"(y) : "r"(a));
+}
 
-// Dequantize one 32-token group (batch slot `slot` of the Q stage at `qs`)
-// into the DQ slot at `dst`: K tile [2][32 rows][64 dims] then V tile, both
-// swizzled like a TMA tile, rows in token order.  V rows of unattended tokens
-// (bit clear in `valid`) are written as zeros so that stale or degenerate
-// data (an fp16 zero point that overflowed to inf) cannot reach P.V.
-__device__ __forceinline__ void dequant_group(uint32_t qs, int slot, uint32_t dst, uint32_t valid, int lane) {
-  const __half2 k1024 = u32_as_h2(0x64006400u);
+// fp16 2^(10 - 2j) in both halves: OR-ing 2-bit field j of a byte (bits 2j,
+// 2j+1 of the half's low byte, whose weight at that exponent is 1) into it
+// gives 2^(10-2j) + code exactly; subtracting it again leaves the code.
+__device__ __forceinline__ uint32_t magic2(int j) { return 0x64006400u - static_cast<uint32_t>(j) * 0x08000800u; }
+
+// Per-lane constants of the quantized path (g = lane / 4, t = lane % 4).
+struct LaneQ {
+  uint32_t mk_lo, mg_lo, mk_hi, mg_hi;  // K: code fields of rows g / g+8 within their byte
+  uint32_t mv, mgv, selv;               // V: code field of dims = g (mod 4), byte selector
+  int tau_lo, tau_hi;                   // tokens (within a 16-token half) of mma rows g, g+8
+  int tv[4];                            // tokens of the P^T k-rows 2t, 2t+1, 2t+8, 2t+9
+  __device__ __forceinline__ explicit LaneQ(int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    // mma row rho = g' + 8h (g' < 8) holds token 4*(g'/2) + ((g'/2 + g'%2 + 2h) % 4):
+    // rows g and g+8 share packed K byte row g/2, and the four tokens of a
+    // lane's P^T fragment are byte row t's, each once.
+    const int jlo = ((g >> 1) + (g & 1)) & 3, jhi = (jlo + 2) & 3;
+    mk_lo = 0x00030003u << (2 * jlo);
+    mg_lo = magic2(jlo);
+    mk_hi = 0x00030003u << (2 * jhi);
+    mg_hi = magic2(jhi);
+    tau_lo = 4 * (g >> 1) + jlo;
+    tau_hi = 4 * (g >> 1) + jhi;
+    mv = 0x00030003u << (2 * (g & 3));
+    mgv = magic2(g & 3);
+    selv = (g >> 2) ? 0x7531u : 0x6420u;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) tv[k] = 4 * t + ((t + k) & 3);
+  }
+};
+
+// Attend to the attended tokens (`mask`) of the quantized group in batch slot
+// `gs` of the Q stage at `qs`.  qrow: this lane's query words Q[head g][32t ..
+// 32t+31] in shared memory (natural order).
+__device__ __forceinline__ void attend_group(WarpAttn& st, uint32_t qrow, const LaneQ& lq, uint32_t qs, int gs,
+                                             uint32_t mask, float scale_log2, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  // ---- per group: query scaled by the K scales, zero-point term, permuted B-fragments
+  uint32_t qp[8][2];
+  float zb0, zb1;  // sum_d z_d * s_d * Q[h][d] for heads 2t, 2t+1
   {
-    // K: lane = (byte row r: tokens 4r..4r+3, channel quarter cq: 32 channels)
-    const int r = lane >> 2, cq = lane & 3;
-    uint32_t w[8], sc[16], zr[16];
-    const uint32_t src = qs + kOffKP + slot * 1024 + r * 128 + 32 * cq;
-    lds128(src, w[0], w[1], w[2], w[3]);
-    lds128(src + 16, w[4], w[5], w[6], w[7]);
+    uint32_t sq[16], zn[16];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      lds128(qs + kOffKS + slot * 256 + 64 * cq + 16 * i, sc[4 * i], sc[4 * i + 1], sc[4 * i + 2], sc[4 * i + 3]);
-      lds128(qs + kOffKZ + slot * 256 + 64 * cq + 16 * i, zr[4 * i], zr[4 * i + 1], zr[4 * i + 2], zr[4 * i + 3]);
+      uint32_t s0, s1, s2, s3, q0, q1, q2, q3;
+      lds128(qs + kOffKS + gs * 256 + 64 * t + 16 * i, s0, s1, s2, s3);
+      lds128(qrow + 16 * i, q0, q1, q2, q3);
+      sq[4 * i] = hmul2u(q0, s0);
+      sq[4 * i + 1] = hmul2u(q1, s1);
+      sq[4 * i + 2] = hmul2u(q2, s2);
+      sq[4 * i + 3] = hmul2u(q3, s3);
+      lds128(qs + kOffKZ + gs * 256 + 64 * t + 16 * i, zn[4 * i], zn[4 * i + 1], zn[4 * i + 2], zn[4 * i + 3]);
     }
-    uint32_t x[16];
-    __half2 nz[16];
+    float zc[4] = {0.f, 0.f, 0.f, 0.f}, zc2[4] = {0.f, 0.f, 0.f, 0.f};  // two chains: half the mma latency
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      x[i] = __byte_perm(w[i >> 1], 0u, (i & 1) ? 0x4342u : 0x4140u);  // [b_lo, 0, b_hi, 0]
-      nz[i] = __hneg2(__hmul2(u32_as_h2(sc[i]), u32_as_h2(zr[i])));
+    for (int kk = 0; kk < 8; ++kk) {
+      // natural k order: k-cols (2t, 2t+1) = channels 32t+4kk+{0,1}, (2t+8, 2t+9) = +{2,3}
+      mma_16816((kk & 1) ? zc2 : zc, zn[2 * kk], zn[2 * kk], zn[2 * kk + 1], zn[2 * kk + 1], sq[2 * kk],
+                sq[2 * kk + 1]);
+      // permuted k order of the code fragments: (2t, 2t+1) = +{0,2}, (2t+8, 2t+9) = +{1,3}
+      qp[kk][0] = __byte_perm(sq[2 * kk], sq[2 * kk + 1], 0x5410);
+      qp[kk][1] = __byte_perm(sq[2 * kk], sq[2 * kk + 1], 0x7632);
     }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t row = 4 * r + j;
-      uint32_t out[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t c = ((x[i] >> (2 * j)) & 0x00030003u) | 0x64006400u;
-        out[i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(c), k1024), u32_as_h2(sc[i]), nz[i]));
-      }
-      // channels 32cq.. = global chunks 4cq..4cq+3: region cq/2, local chunks (4cq & 7)..
-      const uint32_t region = dst + (cq >> 1) * kDqRegion;
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc)
-        sts128(region + swz128(row, ((4 * cq) & 7) + cc), out[4 * cc], out[4 * cc + 1], out[4 * cc + 2],
-               out[4 * cc + 3]);
-    }
+    zb0 = zc[0] + zc2[0];
+    zb1 = zc[1] + zc2[1];
   }
+  // ---- S^T = C.(sQ)^T - z.(sQ)^T for both 16-token halves at once (four
+  // independent mma chains); a half without attended tokens is computed too
+  // (its rows are masked) -- its codes are real, finite data
+  const uint32_t hm[2] = {mask & 0xffffu, mask >> 16};
+  float s[2][4], s2[2][4];
   {
-    // V: lane = token (channels in bytes: byte b holds channels 4b..4b+3)
-    const int tau = lane;
-    const bool ok = (valid >> tau) & 1u;
-    uint32_t w[8];
-    const uint32_t src = qs + kOffVP + slot * 1024 + tau * 32;
-    lds128(src, w[0], w[1], w[2], w[3]);
-    lds128(src + 16, w[4], w[5], w[6], w[7]);
-    uint32_t s01, s23, z01, z23;
-    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(s01), "=r"(s23) : "r"(qs + kOffVS + slot * 256 + tau * 8));
-    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(z01), "=r"(z23) : "r"(qs + kOffVZ + slot * 256 + tau * 8));
-    const __half2 sp[2] = {u32_as_h2(s01), u32_as_h2(s23)};
-    const __half2 nzp[2] = {__hneg2(__hmul2(sp[0], u32_as_h2(z01))), __hneg2(__hmul2(sp[1], u32_as_h2(z23)))};
-    const __half2 quarter_hi = __halves2half2(__float2half_rn(1.f), __float2half_rn(0.25f));
-    const uint32_t vdst = dst + kDqTile;
+    uint32_t kw[2][8];
 #pragma unroll
-    for (int ch = 0; ch < 16; ++ch) {  // 8 channels = bytes 2ch, 2ch+1; group ch / 4
-      const int q = ch >> 2;
-      const __half2 s = (q & 1) ? __high2half2(sp[q >> 1]) : __low2half2(sp[q >> 1]);
-      const __half2 nzq = (q & 1) ? __high2half2(nzp[q >> 1]) : __low2half2(nzp[q >> 1]);
-      uint32_t out[4];
+    for (int hf = 0; hf < 2; ++hf) {
+      s[hf][0] = s[hf][2] = -zb0;
+      s[hf][1] = s[hf][3] = -zb1;
+      s2[hf][0] = s2[hf][1] = s2[hf][2] = s2[hf][3] = 0.f;
+      const uint32_t src = qs + kOffKP + gs * 1024 + (4 * hf + (g >> 1)) * 128 + 32 * t;
+      lds128(src, kw[hf][0], kw[hf][1], kw[hf][2], kw[hf][3]);
+      lds128(src + 16, kw[hf][4], kw[hf][5], kw[hf][6], kw[hf][7]);
+    }
 #pragma unroll
-      for (int bb = 0; bb < 2; ++bb) {
-        const int byte = 2 * ch + bb;
-        const uint32_t k = byte & 3;
-        const uint32_t xb = __byte_perm(w[byte >> 2], 0u, 0x4040u | (k << 8) | k);  // [b, 0, b, 0]
+    for (int kk = 0; kk < 8; ++kk) {
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          // channels 4 byte + 2hh, +1: bits 4hh..+1 (lo) and 4hh+2..+3 (hi, as 4c)
-          const uint32_t c = ((xb >> (4 * hh)) & 0x000C0003u) | 0x64006400u;
-          const __half2 cv = __hmul2(__hsub2(u32_as_h2(c), k1024), quarter_hi);
-          out[2 * bb + hh] = ok ? h2_as_u32(__hfma2(cv, s, nzq)) : 0u;
-        }
+      for (int hf = 0; hf < 2; ++hf) {
+        const uint32_t w = kw[hf][kk], wh = w >> 8;  // bytes: channels 32t+4kk+{0,1,2,3}
+        const uint32_t a0 = hsub2u((w & lq.mk_lo) | lq.mg_lo, lq.mg_lo);
+        const uint32_t a1 = hsub2u((w & lq.mk_hi) | lq.mg_hi, lq.mg_hi);
+        const uint32_t a2 = hsub2u((wh & lq.mk_lo) | lq.mg_lo, lq.mg_lo);
+        const uint32_t a3 = hsub2u((wh & lq.mk_hi) | lq.mg_hi, lq.mg_hi);
+        mma_16816((kk & 1) ? s2[hf] : s[hf], a0, a1, a2, a3, qp[kk][0], qp[kk][1]);
       }
-      sts128(vdst + (ch >> 3) * kDqRegion + swz128(tau, ch & 7), out[0], out[1], out[2], out[3]);
+    }
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[hf][c] += s2[hf][c];
+  }
+  uint32_t pb[2][2];
+  {
+    const bool vlo[2] = {((hm[0] >> lq.tau_lo) & 1u) != 0, ((hm[1] >> lq.tau_lo) & 1u) != 0};
+    const bool vhi[2] = {((hm[0] >> lq.tau_hi) & 1u) != 0, ((hm[1] >> lq.tau_hi) & 1u) != 0};
+    st.softmax_rows<2>(s, vlo, vhi, scale_log2, pb);
+  }
+
+  // ---- O^T += (C - Z)^T.(P*s)^T: channel group G = m-tiles 2G, 2G+1
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    if (!hm[hf]) continue;
+    const uint32_t vrow = qs + kOffVP + gs * 1024 + 16 * hf * 32;
+    uint32_t vs[4][2], vz[4][2];  // scales / zero points of tokens tv[k], channel groups (0,1), (2,3)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int tok = 16 * hf + lq.tv[k];
+      lds64(qs + kOffVS + gs * 256 + tok * 8, vs[k][0], vs[k][1]);
+      lds64(qs + kOffVZ + gs * 256 + tok * 8, vz[k][0], vz[k][1]);
+    }
+    // unattended tokens: scale and zero 0, so that their terms are exactly 0
+    // whatever the stored values (P is 0 there; this keeps inf / NaN out of P.V)
+    bool all_ok = true;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) all_ok &= ((hm[hf] >> lq.tv[k]) & 1u) != 0;
+    if (!__all_sync(0xffffffffu, all_ok)) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (!((hm[hf] >> lq.tv[k]) & 1u)) vs[k][0] = vs[k][1] = vz[k][0] = vz[k][1] = 0u;
+    }
+    uint32_t p01[4], p23[4], z01[4], z23[4];
+#pragma unroll
+    for (int G = 0; G < 4; ++G) {
+      // pb[hf][0] holds P of tokens tv[0], tv[1] (k-rows 2t, 2t+1), pb[hf][1] of tv[2], tv[3]
+      const uint32_t sel = (G & 1) ? 0x7632u : 0x5410u;
+      p01[G] = hmul2u(pb[hf][0], __byte_perm(vs[0][G >> 1], vs[1][G >> 1], sel));
+      p23[G] = hmul2u(pb[hf][1], __byte_perm(vs[2][G >> 1], vs[3][G >> 1], sel));
+      z01[G] = hadd2u(__byte_perm(vz[0][G >> 1], vz[1][G >> 1], sel), lq.mgv);
+      z23[G] = hadd2u(__byte_perm(vz[2][G >> 1], vz[3][G >> 1], sel), lq.mgv);
+    }
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {  // m-tiles 4*half .. +3 = packed bytes 16*half .. +15
+      uint32_t vw[4][4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        lds128(vrow + lq.tv[k] * 32 + 16 * half, vw[k][0], vw[k][1], vw[k][2], vw[k][3]);
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int j = 4 * half + jj, G = j >> 1;
+        // word jj: bytes 4j..4j+3 = dims 16j..16j+15; dim 16j+g is byte g/4 field g%4, dim 16j+g+8 byte 2+g/4
+        const uint32_t x01 = __byte_perm(vw[0][jj], vw[1][jj], lq.selv);
+        const uint32_t x23 = __byte_perm(vw[2][jj], vw[3][jj], lq.selv);
+        // A = c - z (exact): (magic + c) - (magic + z)
+        const uint32_t a0 = hsub2u((x01 & lq.mv) | lq.mgv, z01[G]);
+        const uint32_t a1 = hsub2u(((x01 >> 8) & lq.mv) | lq.mgv, z01[G]);
+        const uint32_t a2 = hsub2u((x23 & lq.mv) | lq.mgv, z23[G]);
+        const uint32_t a3 = hsub2u(((x23 >> 8) & lq.mv) | lq.mgv, z23[G]);
+        mma_16816(st.acc[j], a0, a1, a2, a3, p01[G], p23[G]);
+      }
     }
   }
 }
@@ -367,48 +431,37 @@ __device__ __forceinline__ void zero_invalid_v_rows(uint32_t vbase, uint32_t reg
   __syncwarp();
 }
 
-__device__ __forceinline__ void mma_warps_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kMmaWarps * 32) : "memory");
-}
+__device__ __forceinline__ void cwarps_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory"); }
 
-// Attended-token mask (bit j = token j) of batch slot `slot` of Q-batch `b`.
-__device__ __forceinline__ uint32_t group_mask(const KParams& p, const KiviMeta& m, int b, int slot) {
-  uint32_t mask = 0;
-  const int v = kBatchGroups * b + slot;
-  if (v == 0) return m.n_sink >= 32 ? 0xffffffffu : ((1u << m.n_sink) - 1u);
-  if (v > p.n_groups) return 0;
-  const int age = grp_age(p, m, v - 1);
-  if (age >= m.n_grp) return 0;
-  const int first = m.tok_skip - 32 * age;  // tokens below this one are not attended
-  if (first <= 0) return 0xffffffffu;
-  if (first >= 32) return 0;
-  mask = ~((1u << first) - 1u);
-  return mask;
-}
-
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     kivi_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                        const KParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  grid_launch_dependents();
+  grid_dependency_wait();  // the cache and q may come from the previous kernel of the stream
+  if (smem_u32(smem_raw) & 1023u) {  // TMA tile destinations need 1024-byte alignment
+    if (threadIdx.x == 0) set_error(p.err, NSA_ERR_ALIGN);
+    return;
+  }
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t unit = blockIdx.x / p.ppu;
+  const int piece = static_cast<int>(blockIdx.x % p.ppu);
+  // this piece's items [t_begin, t_end): item 0 = Q-batch 0, items 1..n_ft =
+  // F-tiles 0..n_ft-1, item n_ft + b = Q-batch b (b >= 1)
+  const int t_begin = piece * p.items / p.ppu, t_end = (piece + 1) * p.items / p.ppu;
+  const bool has_b0 = t_begin == 0 && t_end > 0;
+  const int f_begin = max(t_begin, 1) - 1, f_end = min(t_end, p.n_ft + 1) - 1;
+  const int b_begin = max(max(t_begin, p.n_ft + 1) - p.n_ft, 1), b_end = t_end - p.n_ft;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kFStages; ++s) {
       mbar_init(smem_u32(&sm.f_full[s]), 1);
-      mbar_init(smem_u32(&sm.f_empty[s]), kMmaWarps);
+      mbar_init(smem_u32(&sm.f_empty[s]), kCWarps);
     }
     for (int s = 0; s < kQStages; ++s) {
       mbar_init(smem_u32(&sm.q_full[s]), 1);
-      mbar_init(smem_u32(&sm.q_empty[s]), kDqWarps);
-    }
-    for (int s = 0; s < kDqSlots; ++s) {
-      mbar_init(smem_u32(&sm.dq_full[s]), 1);
-      mbar_init(smem_u32(&sm.dq_empty[s]), kMmaWarps);
-    }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(smem_u32(&sm.qv_full[s]), 1);
-      mbar_init(smem_u32(&sm.qv_empty[s]), kMmaWarps);
+      mbar_init(smem_u32(&sm.q_empty[s]), kCWarps);
     }
     fence_barrier_init();
   }
@@ -419,261 +472,214 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
-      uint32_t nf = 0, nq = 0, nv = 0;  // items issued per ring
-      PieceIter it(p);
-      Piece pc;
+      // Q-batch b into stage s: the sink group (batch 0) and window groups p0..p1-1
+      auto issue_batch = [&](int b, uint32_t s) {
+        const uint32_t fb = smem_u32(&sm.q_full[s]);
+        const uint32_t sd = smem_u32(sm.qb[s]);
+        const int p0 = b == 0 ? 0 : kBatchGroups * b - 1;  // batch slot v holds group v - 1
+        const int p1 = min(p.n_groups, kBatchGroups * b + kBatchGroups - 1);
+        const int so = p0 + 1 - kBatchGroups * b;
+        const uint32_t ng = p1 > p0 ? p1 - p0 : 0;
+        mbar_arrive_expect_tx(fb, (b == 0 ? 3072u : 0u) + ng * 3072u);
+        if (ng) {
+          const int64_t gbase = unit * p.n_groups + p0;
+          bulk_load(sd + kOffKP + so * 1024, p.kw_p + gbase * 1024, ng * 1024, fb);
+          bulk_load(sd + kOffKS + so * 256, p.kw_s + gbase * 128, ng * 256, fb);
+          bulk_load(sd + kOffKZ + so * 256, p.kw_z + gbase * 128, ng * 256, fb);
+          bulk_load(sd + kOffVP + so * 1024, p.vw_p + gbase * 1024, ng * 1024, fb);
+          bulk_load(sd + kOffVS + so * 256, p.vw_s + gbase * 128, ng * 256, fb);
+          bulk_load(sd + kOffVZ + so * 256, p.vw_z + gbase * 128, ng * 256, fb);
+        }
+        if (b == 0) {
+          bulk_load(sd + kOffKP, p.ks_p + unit * 1024, 1024, fb);
+          bulk_load(sd + kOffKS, p.ks_s + unit * 128, 256, fb);
+          bulk_load(sd + kOffKZ, p.ks_z + unit * 128, 256, fb);
+          bulk_load(sd + kOffVP, p.vs_p + unit * 1024, 1024, fb);
+          bulk_load(sd + kOffVS, p.vs_s + unit * 128, 256, fb);
+          bulk_load(sd + kOffVZ, p.vs_z + unit * 128, 256, fb);
+        }
+      };
+      uint32_t nq = 0;
+      if (has_b0) issue_batch(0, nq++);  // first use of stage 0: nothing to wait for
       bool ok = true;
-      while (ok && it.next(p, pc)) {
-        const int64_t u = pc.unit;
-        const KiviMeta meta = make_meta(p, u);
-        {
-          const uint32_t s = nv % 2, ph = (nv / 2) & 1;
-          ++nv;
-          if (!mbar_wait(smem_u32(&sm.qv_empty[s]), ph ^ 1, p.err)) break;
-          sm.meta[s] = meta;  // published by the arrive below (release)
-          mbar_arrive_expect_tx(smem_u32(&sm.qv_full[s]), kQBytes);
-          bulk_load(smem_u32(sm.q[s]), p.q + u * kGroupHeads * kHeadDim, kQBytes, smem_u32(&sm.qv_full[s]));
-        }
-        // Quantized batches first when they all fit in the Q ring (their
-        // dequantization then overlaps the residual tiles).  Otherwise the
-        // residual tiles go first: the MMA warps consume a piece's residual
-        // tiles before its groups, so a producer stuck on a full Q ring must
-        // not hold back residual tiles they wait for.
-        int live_q = 0;
-        for (int64_t t = pc.t_begin; t < pc.t_end; ++t)
-          if (t < p.n_qb && item_live(p, meta, static_cast<int>(t))) ++live_q;
-        const bool q_first = live_q <= kQStages;
-        for (int pass = 0; pass < 2 && ok; ++pass) {
-          for (int64_t t = pc.t_begin; t < pc.t_end; ++t) {
-            const int itm = static_cast<int>(t);
-            const bool is_q = itm < p.n_qb;
-            if (is_q != ((pass == 0) == q_first) || !item_live(p, meta, itm)) continue;
-            if (is_q) {
-              const uint32_t s = nq % kQStages, ph = (nq / kQStages) & 1;
-              ++nq;
-              if (!mbar_wait(smem_u32(&sm.q_empty[s]), ph ^ 1, p.err)) { ok = false; break; }
-              const uint32_t fb = smem_u32(&sm.q_full[s]);
-              const uint32_t sd = smem_u32(sm.qb[s]);
-              sm.qhdr[s].meta = meta;
-              sm.qhdr[s].item = itm;
-              sm.qhdr[s].end = 0;
-              const int b = itm;
-              const bool has_sink = (b == 0);
-              const int p0 = b == 0 ? 0 : kBatchGroups * b - 1;
-              const int p1 = min(p.n_groups, kBatchGroups * b + kBatchGroups - 1);
-              const int so = p0 + 1 - kBatchGroups * b;  // batch slot of group p0
-              const uint32_t ng = p1 > p0 ? p1 - p0 : 0;
-              mbar_arrive_expect_tx(fb, (has_sink ? 3072u : 0u) + ng * 3072u);
-              if (has_sink) {
-                bulk_load(sd + kOffKP, p.ks_p + u * 1024, 1024, fb);
-                bulk_load(sd + kOffKS, p.ks_s + u * 128, 256, fb);
-                bulk_load(sd + kOffKZ, p.ks_z + u * 128, 256, fb);
-                bulk_load(sd + kOffVP, p.vs_p + u * 1024, 1024, fb);
-                bulk_load(sd + kOffVS, p.vs_s + u * 128, 256, fb);
-                bulk_load(sd + kOffVZ, p.vs_z + u * 128, 256, fb);
-              }
-              if (ng) {
-                const int64_t gbase = u * p.n_groups + p0;
-                bulk_load(sd + kOffKP + so * 1024, p.kw_p + gbase * 1024, ng * 1024, fb);
-                bulk_load(sd + kOffKS + so * 256, p.kw_s + gbase * 128, ng * 256, fb);
-                bulk_load(sd + kOffKZ + so * 256, p.kw_z + gbase * 128, ng * 256, fb);
-                bulk_load(sd + kOffVP + so * 1024, p.vw_p + gbase * 1024, ng * 1024, fb);
-                bulk_load(sd + kOffVS + so * 256, p.vw_s + gbase * 128, ng * 256, fb);
-                bulk_load(sd + kOffVZ + so * 256, p.vw_z + gbase * 128, ng * 256, fb);
-              }
-            } else {
-              const uint32_t s = nf % kFStages, ph = (nf / kFStages) & 1;
-              ++nf;
-              if (!mbar_wait(smem_u32(&sm.f_empty[s]), ph ^ 1, p.err)) { ok = false; break; }
-              const uint32_t fb = smem_u32(&sm.f_full[s]);
-              const uint32_t sd = smem_u32(sm.f[s]);
-              mbar_arrive_expect_tx(fb, kFStageBytes);
-              const int row = (itm - p.n_qb) * kTile;
-              const int uu = static_cast<int>(u);
-              tma_load_3d(sd, &tmK, fb, 0, row, uu);
-              tma_load_3d(sd + kRegionBytes, &tmK, fb, 64, row, uu);
-              tma_load_3d(sd + kTileBytes, &tmV, fb, 0, row, uu);
-              tma_load_3d(sd + kTileBytes + kRegionBytes, &tmV, fb, 64, row, uu);
-            }
-          }
-        }
+      uint32_t nf = 0;
+      for (int f = f_begin; f < f_end && ok; ++f) {
+        const uint32_t s = nf % kFStages, ph = (nf / kFStages) & 1;
+        ++nf;
+        if (!mbar_wait(smem_u32(&sm.f_empty[s]), ph ^ 1, p.err)) { ok = false; break; }
+        const uint32_t fb = smem_u32(&sm.f_full[s]);
+        const uint32_t sd = smem_u32(sm.f[s]);
+        mbar_arrive_expect_tx(fb, kFStageBytes);
+        const int uu = static_cast<int>(unit);
+        tma_load_4d(sd, &tmK, fb, 0, f * kFRows, 0, uu);
+        tma_load_4d(sd + kFTile, &tmV, fb, 0, f * kFRows, 0, uu);
       }
-      if (ok) {
-        // sentinel for the dequantizers
+      const KiviMeta meta = make_meta(p, unit);
+      for (int b = b_begin; b < b_end && ok; ++b) {
+        if (!batch_live(p, meta, b)) continue;
         const uint32_t s = nq % kQStages, ph = (nq / kQStages) & 1;
-        if (mbar_wait(smem_u32(&sm.q_empty[s]), ph ^ 1, p.err)) {
-          sm.qhdr[s].end = 1;
-          mbar_arrive(smem_u32(&sm.q_full[s]));
-        }
+        ++nq;
+        if (!mbar_wait(smem_u32(&sm.q_empty[s]), ph ^ 1, p.err)) { ok = false; break; }
+        issue_batch(b, s);
       }
     }
     return;
   }
 
-  if (warp >= kMmaWarps) {
-    // ------------------------------------------------------- dequantizers
-    const int dw = warp - kMmaWarps;
-    uint32_t nq = 0, ng = 0;  // Q stages consumed; live groups seen (all dequant warps count alike)
-    for (;;) {
+  // -------------------------------------------------------------- consumers
+  // A timed-out wait sets `aborted`: the warp then stops waiting (the error
+  // word is already set) but keeps its schedule of named barriers.
+  const int g = lane >> 2, t = lane & 3;
+  const KiviMeta meta = make_meta(p, unit);
+  const LaneQ lq(lane);
+  bool aborted = false;
+  {
+    const int ct = threadIdx.x;  // 128 consumer threads bring 16 bytes of the query each
+    const int row = ct >> 4, col = (ct & 15) * 8;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.q + (unit * kGroupHeads + row) * kHeadDim + col));
+    sts128(smem_u32(&sm.qpad[row][col]), v.x, v.y, v.z, v.w);
+    cwarps_sync();
+  }
+  WarpAttn st;
+  st.reset();
+  const uint32_t qpad = smem_u32(sm.qpad);
+  const uint32_t qrow = qpad + g * (kQPadStride * 2) + 64 * t;
+  JobSched js;
+  uint32_t nf = 0, nq = 0;
+  // phase 0: Q-batch 0; phase 1: the F-tiles; phase 2: Q-batches b_begin ..
+  // (one loop so that each consumer path is instantiated once)
+#pragma unroll 1
+  for (int phase = 0; phase < 3; ++phase) {
+    if (phase == 1) {
+#pragma unroll 1
+      for (int f = f_begin; f < f_end; ++f) {
+        const uint32_t s = nf % kFStages, ph = (nf / kFStages) & 1;
+        ++nf;
+        if (!aborted && !mbar_wait(smem_u32(&sm.f_full[s]), ph, p.err)) aborted = true;
+        const uint32_t sd = smem_u32(sm.f[s]);
+#pragma unroll 1
+        for (int hf = 0; hf < kFRows / 16; ++hf) {
+          const int r0 = f * kFRows + 16 * hf;
+          const bool v_lo = res_slot_valid(p, meta, r0 + g);
+          const bool v_hi = res_slot_valid(p, meta, r0 + g + 8);
+          if (!__any_sync(0xffffffffu, v_lo || v_hi)) continue;
+          if (js.take(kCostF) != warp) continue;
+          zero_invalid_v_rows(sd + kFTile, kFRegion, 16 * hf, v_lo, v_hi, lane);
+          st.load_q(qpad, lane, kQPadStride * 2);  // reloaded here: not held across the quantized path
+          st.consume16(sd, sd + kFTile, kFRegion, 16 * hf, v_lo, v_hi, p.scale_log2, lane);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sm.f_empty[s]));
+      }
+      continue;
+    }
+    const int lo = phase == 0 ? 0 : b_begin, hi = phase == 0 ? (has_b0 ? 1 : 0) : b_end;
+#pragma unroll 1
+    for (int b = lo; b < hi; ++b) {
+      if (!batch_live(p, meta, b)) continue;
       const uint32_t s = nq % kQStages, ph = (nq / kQStages) & 1;
       ++nq;
-      if (!mbar_wait(smem_u32(&sm.q_full[s]), ph, p.err)) return;
-      const QHeader hdr = sm.qhdr[s];
-      if (hdr.end) return;
+      if (!aborted && !mbar_wait(smem_u32(&sm.q_full[s]), ph, p.err)) aborted = true;
       const uint32_t qs = smem_u32(sm.qb[s]);
-      for (int slot = 0; slot < kBatchGroups; ++slot) {
-        const uint32_t mask = group_mask(p, hdr.meta, hdr.item, slot);
+#pragma unroll 1
+      for (int gs = 0; gs < kBatchGroups; ++gs) {
+        const uint32_t mask = group_mask(p, meta, b, gs);
         if (!mask) continue;
-        const uint32_t n = ng++;
-        if (static_cast<int>(n % kDqWarps) != dw) continue;
-        const uint32_t ds = dw, dph = (n / kDqWarps) & 1;
-        if (!mbar_wait(smem_u32(&sm.dq_empty[ds]), dph ^ 1, p.err)) return;
-        dequant_group(qs, slot, smem_u32(sm.dq[ds]), mask, lane);
-        if (lane == 0) sm.dq_mask[ds] = mask;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&sm.dq_full[ds]));
+        const int halves = ((mask & 0xffffu) ? 1 : 0) + ((mask >> 16) ? 1 : 0);
+        if (js.take(kCostGroup + kCostGroupHalf * halves) != warp) continue;
+        attend_group(st, qrow, lq, qs, gs, mask, p.scale_log2, lane);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&sm.q_empty[s]));
     }
   }
 
-  // -------------------------------------------------------------- MMA warps
-  // A timed-out wait sets `aborted`: the warp then stops waiting (the error
-  // word is already set) but keeps its schedule of named barriers.
-  const int g = lane >> 2;
-  uint32_t nv = 0, nf = 0, ng = 0, job = 0;
-  bool aborted = false;
-  WarpAttn st;
-  PieceIter it(p);
-  Piece pc;
-  while (it.next(p, pc)) {
-    const uint32_t vs = nv % 2, vph = (nv / 2) & 1;
-    ++nv;
-    if (!aborted && !mbar_wait(smem_u32(&sm.qv_full[vs]), vph, p.err)) aborted = true;
-    st.load_q(smem_u32(sm.q[vs]), lane);
-    const KiviMeta meta = sm.meta[vs];
-    __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(&sm.qv_empty[vs]));
-    st.reset();
-    // residual tiles first, then the dequantized groups (the producer issued
-    // the quantized batches first so their dequantization overlaps)
-    for (int64_t t = pc.t_begin; t < pc.t_end; ++t) {
-      const int itm = static_cast<int>(t);
-      if (itm < p.n_qb || !item_live(p, meta, itm)) continue;
-      const uint32_t s = nf % kFStages, ph = (nf / kFStages) & 1;
-      ++nf;
-      if (!aborted && !mbar_wait(smem_u32(&sm.f_full[s]), ph, p.err)) aborted = true;
-      const uint32_t sd = smem_u32(sm.f[s]);
-      const int r0 = (itm - p.n_qb) * kTile + 16 * warp;
-      const bool v_lo = res_slot_valid(p, meta, r0 + g);
-      const bool v_hi = res_slot_valid(p, meta, r0 + g + 8);
-      if (__any_sync(0xffffffffu, v_lo || v_hi)) {
-        zero_invalid_v_rows(sd + kTileBytes, kRegionBytes, 16 * warp, v_lo, v_hi, lane);
-        st.consume16(sd, sd + kTileBytes, kRegionBytes, 16 * warp, v_lo, v_hi, p.scale_log2, lane);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sm.f_empty[s]));
-    }
-    for (int64_t t = pc.t_begin; t < pc.t_end; ++t) {
-      const int itm = static_cast<int>(t);
-      if (itm >= p.n_qb || !item_live(p, meta, itm)) continue;
-      for (int slot = 0; slot < kBatchGroups; ++slot) {
-        if (!group_mask(p, meta, itm, slot)) continue;
-        const uint32_t n = ng++;
-        const uint32_t ds = n % kDqWarps, dph = (n / kDqWarps) & 1;  // group n is in its dequantizer's slot
-        if (!aborted && !mbar_wait(smem_u32(&sm.dq_full[ds]), dph, p.err)) aborted = true;
-        const uint32_t mask = sm.dq_mask[ds];
-        const uint32_t dbase = smem_u32(sm.dq[ds]);
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          const uint32_t hm = (mask >> (16 * hf)) & 0xffffu;
-          if (!hm) continue;
-          if ((job++ % kMmaWarps) != static_cast<uint32_t>(warp)) continue;
-          st.consume16(dbase, dbase + kDqTile, kDqRegion, 16 * hf, (hm >> g) & 1u, (hm >> (g + 8)) & 1u,
-                       p.scale_log2, lane);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&sm.dq_empty[ds]));
-      }
-    }
-
-    // ---- epilogue: merge the 4 MMA warps, write the output or a partial
-    warp_publish(st, sm.ep, warp, lane);
-    mma_warps_sync();
-    const int ct = threadIdx.x;  // 0..127
-    const int hh = ct >> 4, d0 = (ct & 15) * 8;
-    float o[8], lse;
-    {
-      float o4[4];
-      merge_warps(sm.ep, hh, d0, o4, lse);
-      for (int i = 0; i < 4; ++i) o[i] = o4[i];
-      merge_warps(sm.ep, hh, d0 + 4, o4, lse);
-      for (int i = 0; i < 4; ++i) o[4 + i] = o4[i];
-    }
-    __half* out = p.o + pc.unit * kGroupHeads * kHeadDim;
-    if (pc.n_pieces == 1) {
-      const float a[4] = {o[0], o[1], o[2], o[3]}, b[4] = {o[4], o[5], o[6], o[7]};
-      store_half4(out + hh * kHeadDim + d0, a);
-      store_half4(out + hh * kHeadDim + d0 + 4, b);
-    } else {
-      const int64_t pidx = pc.unit * p.max_pieces + pc.slot;
-      float* po = p.part_o + (pidx * kGroupHeads + hh) * kHeadDim + d0;
-      reinterpret_cast<float4*>(po)[0] = make_float4(o[0], o[1], o[2], o[3]);
-      reinterpret_cast<float4*>(po)[1] = make_float4(o[4], o[5], o[6], o[7]);
-      if ((ct & 15) == 0) p.part_lse[pidx * kGroupHeads + hh] = lse;
-      __threadfence();
-      mma_warps_sync();
-      if (ct == 0) sm.ep.ticket = atomicAdd(p.counters + pc.unit, 1);
-      mma_warps_sync();
-      if (sm.ep.ticket == pc.n_pieces - 1) {
-        __threadfence();
-        const int64_t base = pc.unit * p.max_pieces;
-        combine_pieces(p.part_lse + base * kGroupHeads, p.part_o + base * kGroupHeads * kHeadDim, pc.n_pieces, out,
-                       warp * (kGroupHeads / kMmaWarps), kGroupHeads / kMmaWarps, lane);
-        if (ct == 0) p.counters[pc.unit] = 0;
-      }
-    }
-    mma_warps_sync();
+  // ---- epilogue: merge the 4 warps (the F ring is reused once all have finished)
+  cwarps_sync();
+  warp_publish(st, sm.ep, warp, lane);
+  cwarps_sync();
+  const int ct = threadIdx.x;  // 0..127
+  const int hh = ct >> 4, d0 = (ct & 15) * 8;
+  float o[8], lse;
+  {
+    float o4[4];
+    merge_warps(sm.ep, hh, d0, o4, lse);
+    for (int i = 0; i < 4; ++i) o[i] = o4[i];
+    merge_warps(sm.ep, hh, d0 + 4, o4, lse);
+    for (int i = 0; i < 4; ++i) o[4 + i] = o4[i];
+  }
+  __half* out = p.o + unit * kGroupHeads * kHeadDim;
+  if (p.ppu == 1) {
+    const float a[4] = {o[0], o[1], o[2], o[3]}, b[4] = {o[4], o[5], o[6], o[7]};
+    store_half4(out + hh * kHeadDim + d0, a);
+    store_half4(out + hh * kHeadDim + d0 + 4, b);
+    return;
+  }
+  const int64_t pidx = unit * p.ppu + piece;
+  float* po = p.part_o + (pidx * kGroupHeads + hh) * kHeadDim + d0;
+  reinterpret_cast<float4*>(po)[0] = make_float4(o[0], o[1], o[2], o[3]);
+  reinterpret_cast<float4*>(po)[1] = make_float4(o[4], o[5], o[6], o[7]);
+  if ((ct & 15) == 0) p.part_lse[pidx * kGroupHeads + hh] = lse;
+  __threadfence();
+  cwarps_sync();
+  if (ct == 0) sm.ep.ticket = atomicAdd(p.counters + unit, 1);
+  cwarps_sync();
+  if (sm.ep.ticket == p.ppu - 1) {
+    __threadfence();
+    const int64_t base = unit * p.ppu;
+    combine_pieces(p.part_lse + base * kGroupHeads, p.part_o + base * kGroupHeads * kHeadDim, p.ppu, out,
+                   warp * (kGroupHeads / kCWarps), kGroupHeads / kCWarps, lane);
+    if (ct == 0) p.counters[unit] = 0;
   }
 }
 
-constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
-
 struct Plan {
-  int64_t n_units, items, total;
-  int n_qb, n_ft, n_ctas, max_pieces, unit_aligned;
+  int64_t n_units, grid;
+  int n_qb, n_ft, items, ppu;
 };
+
+// CTA slots of the current device (resident CTAs per SM x SMs); sets the
+// kernel's shared-memory limit on first use per device.
+int64_t cta_slots() {
+  static int64_t slots[64] = {0};
+  const DeviceInfo& d = current_device();
+  const int dev = d.device;
+  const int sms = d.sm_count > 0 ? d.sm_count : 148;
+  if (dev < 0 || dev >= 64) return int64_t(sms) * kCtasPerSm;
+  if (!slots[dev]) {
+    int per_sm = 0;
+    if (cudaFuncSetAttribute(kivi_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes)) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kivi_decode_kernel, kThreads, kSmemBytes) !=
+            cudaSuccess ||
+        per_sm < 1) {
+      cudaGetLastError();
+      per_sm = 1;
+    }
+    slots[dev] = int64_t(sms) * per_sm;
+  }
+  return slots[dev];
+}
 
 Plan plan(int64_t n_units, int n_groups, int res_cap) {
   Plan s;
   s.n_units = n_units;
   s.n_qb = (n_groups + 1 + kBatchGroups - 1) / kBatchGroups;
-  s.n_ft = (res_cap + kTile - 1) / kTile;
+  s.n_ft = (res_cap + kFRows - 1) / kFRows;
   s.items = s.n_qb + s.n_ft;
-  s.total = n_units * s.items;
-  const int sms = current_device().sm_count > 0 ? current_device().sm_count : 148;
-  s.n_ctas = static_cast<int>(s.total < sms ? (s.total > 0 ? s.total : 1) : sms);
-  const char* env = getenv("NSA_SPLIT_MODE");
-  const int64_t per_cta = (n_units + sms - 1) / sms;
-  bool whole = n_units >= sms && (s.items <= 32 || per_cta * sms * 4 <= n_units * 5);
-  if (env && env[0] == 's') whole = false;
-  if (env && env[0] == 'u' && n_units >= sms) whole = true;
-  s.unit_aligned = whole ? 1 : 0;
-  if (whole) {
-    s.n_ctas = sms;
-    s.max_pieces = 1;
-  } else {
-    int64_t mp = (s.items * s.n_ctas + s.total - 1) / s.total + 1;
-    if (mp > s.items) mp = s.items;
-    s.max_pieces = static_cast<int>(mp);
-  }
+  // fewer units than CTA slots: split each unit's items so that the slots fill
+  const int64_t slots = cta_slots();
+  int64_t ppu = (n_units > 0 && n_units < slots) ? slots / n_units : 1;
+  if (ppu > s.items) ppu = s.items;
+  if (ppu < 1) ppu = 1;
+  s.ppu = static_cast<int>(ppu);
+  s.grid = n_units * ppu;
   return s;
 }
 
 size_t ws_bytes(const Plan& s) {
   const size_t counters = ((s.n_units * sizeof(int)) + 255) & ~size_t(255);
-  const size_t pieces = static_cast<size_t>(s.n_units) * s.max_pieces;
+  const size_t pieces = static_cast<size_t>(s.n_units) * s.ppu;
   const size_t lse = ((pieces * kGroupHeads * sizeof(float)) + 255) & ~size_t(255);
   return counters + lse + pieces * kGroupHeads * kHeadDim * sizeof(float);
 }
@@ -685,9 +691,10 @@ int launch(KParams& p, const Plan& s, const void* k_res, const void* v_res, void
   if (!ws || wsb < need)
     return fail(NSA_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, ws ? wsb : size_t(0));
   if (!aligned16(ws)) return fail(NSA_ERR_ALIGN, "workspace must be 16-byte aligned");
+  if (s.grid > 0x7fffffff) return fail(NSA_ERR_UNSUPPORTED, "too many units for one launch");
   uint8_t* w = static_cast<uint8_t*>(ws);
   const size_t counters = ((s.n_units * sizeof(int)) + 255) & ~size_t(255);
-  const size_t pieces = static_cast<size_t>(s.n_units) * s.max_pieces;
+  const size_t pieces = static_cast<size_t>(s.n_units) * s.ppu;
   const size_t lse = ((pieces * kGroupHeads * sizeof(float)) + 255) & ~size_t(255);
   p.counters = reinterpret_cast<int*>(w);
   p.part_lse = reinterpret_cast<float*>(w + counters);
@@ -695,33 +702,26 @@ int launch(KParams& p, const Plan& s, const void* k_res, const void* v_res, void
   p.n_units = s.n_units;
   p.n_qb = s.n_qb;
   p.n_ft = s.n_ft;
-  p.tiles_per_unit = s.items;
-  p.total_tiles = s.total;
-  p.n_ctas = s.n_ctas;
-  p.unit_aligned = s.unit_aligned;
-  p.max_pieces = s.max_pieces;
+  p.items = s.items;
+  p.ppu = s.ppu;
   p.err = device_error_word();
   if (!p.err) return fail(NSA_ERR_CUDA, "device error word unavailable");
 
+  // residual [units][res_cap][128] viewed as [units][2 halves][res_cap][64] (dims
+  // innermost first): one box brings 80 slots x both 64-dim halves, each half a
+  // 128-byte-swizzled region of 80 rows
   CUtensorMap mk, mv;
-  const uint64_t dims[3] = {static_cast<uint64_t>(kHeadDim), static_cast<uint64_t>(p.res_cap),
-                            static_cast<uint64_t>(s.n_units)};
-  const uint64_t strides[2] = {kHeadDim * 2, static_cast<uint64_t>(p.res_cap) * kHeadDim * 2};
-  const uint32_t box[3] = {64, kTile, 1};
-  int rc = encode_tiled(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, k_res, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  const uint64_t dims[4] = {64, static_cast<uint64_t>(p.res_cap), 2, static_cast<uint64_t>(s.n_units)};
+  const uint64_t strides[3] = {kHeadDim * 2, 128, static_cast<uint64_t>(p.res_cap) * kHeadDim * 2};
+  const uint32_t box[4] = {64, kFRows, 2, 1};
+  int rc = encode_tiled(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, k_res, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = encode_tiled(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, v_res, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  rc = encode_tiled(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, v_res, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  static bool attr_set[64] = {false};
-  const int dev = current_device().device;
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kivi_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kSmemBytes));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-    attr_set[dev] = true;
-  }
-  kivi_decode_kernel<<<s.n_ctas, kThreads, kSmemBytes, stream>>>(mk, mv, p);
-  cudaError_t e = cudaGetLastError();
+  cta_slots();  // sets the shared-memory limit
+  cudaError_t e = launch_kernel(kivi_decode_kernel, dim3(static_cast<unsigned>(s.grid)), dim3(kThreads), kSmemBytes,
+                                stream, mk, mv, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? NSA_OK : cuda_fail(e, "kivi_decode_kernel launch");
 }
 

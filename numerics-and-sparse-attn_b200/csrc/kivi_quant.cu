@@ -13,6 +13,7 @@
 // codes computed with the float32 scale.
 #include <cuda_fp16.h>
 
+#include "common.cuh"
 #include "host_util.h"
 
 namespace nsa {
@@ -178,6 +179,8 @@ __global__ void kivi_append_kernel(const __half* __restrict__ new_k, const __hal
                                    __half* __restrict__ k_res, __half* __restrict__ v_res,
                                    int64_t* __restrict__ unit_lens, int sink, int residual, int n_groups) {
   constexpr int D = 128;
+  grid_launch_dependents();
+  grid_dependency_wait();  // the previous kernel may still read this cache
   const int64_t u = blockIdx.x;
   const int c = threadIdx.x;
   const int64_t pos = unit_lens[u];
@@ -388,7 +391,8 @@ int nsa_kivi_append(const nsa_kivi_stream_cache* cache, const void* new_k, const
   if (rc) return rc;
   const int64_t units = c.batch * c.n_kv_heads;
   if (units == 0) return NSA_OK;
-  kivi_append_kernel<<<static_cast<unsigned>(units), 128, 0, stream>>>(
+  cudaError_t e = launch_kernel(
+      kivi_append_kernel, dim3(static_cast<unsigned>(units)), dim3(128), 0, stream,
       static_cast<const __half*>(new_k), static_cast<const __half*>(new_v), static_cast<__half*>(c.sink_k),
       static_cast<__half*>(c.sink_v), static_cast<uint8_t*>(c.k_sink_packed), static_cast<__half*>(c.k_sink_scale),
       static_cast<__half*>(c.k_sink_zero), static_cast<uint8_t*>(c.v_sink_packed),
@@ -397,7 +401,7 @@ int nsa_kivi_append(const nsa_kivi_stream_cache* cache, const void* new_k, const
       static_cast<uint8_t*>(c.v_win_packed), static_cast<__half*>(c.v_win_scale), static_cast<__half*>(c.v_win_zero),
       static_cast<__half*>(c.k_res), static_cast<__half*>(c.v_res), c.unit_lens, static_cast<int>(c.sink),
       static_cast<int>(c.residual), static_cast<int>(c.n_groups));
-  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? NSA_OK : cuda_fail(e, "kivi_append launch");
 }
 
