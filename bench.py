@@ -153,7 +153,8 @@ class Workload:
             self.ring_head = torch.full((batch,), (self.seq_len - S) % self.window, dtype=torch.int32,
                                         device=device)
         self.out = [None] * self.n_layers
-        self.launches_per_step = 2 if name == "kivi" else 1  # kivi: append kernel + attention kernel
+        # kivi: one launch when the decode kernel also appends (every unit has its own CTA), else append + decode
+        self.launches_per_step = self.layers[0].step_launches() if name == "kivi" else 1
 
     def step(self, i: int, q=None, new_k=None, new_v=None):
         j = i % self.n_layers

@@ -194,6 +194,16 @@ int nsa_kivi_append(const nsa_kivi_stream_cache* cache, const void* new_k, const
 size_t nsa_kivi_stream_workspace_bytes(const nsa_kivi_stream_cache* cache);
 int nsa_kivi_stream_decode(const nsa_kivi_stream_cache* cache, const void* q, void* o, float sm_scale,
                            void* workspace, size_t workspace_bytes, nsa_stream_t stream);
+/* One decode step: nsa_kivi_append(new_k, new_v) then nsa_kivi_stream_decode(q),
+ * with the same results and cache state.  When every unit is decoded by a
+ * single CTA (units >= half the CTA slots) both run in one launch: the
+ * decode's CTA of each unit stores the token, quantizes a completed group or
+ * the sink group itself, and attends over its staged copies.  Same workspace
+ * as nsa_kivi_stream_decode.  No reference counterpart (the reference has no
+ * append path). */
+int nsa_kivi_stream_decode_step(const nsa_kivi_stream_cache* cache, const void* new_k, const void* new_v,
+                                const void* q, void* o, float sm_scale, void* workspace, size_t workspace_bytes,
+                                nsa_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -52,6 +52,7 @@ PROTOTYPES = {
     "nsa_kivi_append": (_INT, [_P, _P, _P, _P]),
     "nsa_kivi_stream_workspace_bytes": (_SZ, [_P]),
     "nsa_kivi_stream_decode": (_INT, [_P, _P, _P, _F, _P, _SZ, _P]),
+    "nsa_kivi_stream_decode_step": (_INT, [_P, _P, _P, _P, _P, _F, _P, _SZ, _P]),
 }
 
 _lock = threading.Lock()

@@ -154,6 +154,50 @@ struct WarpAttn {
       }
     }
   }
+
+  // Consume N blocks of 16 tokens, rows [row0, row0 + 16N) of a swizzled tile
+  // (regions `region_bytes` apart), with one softmax step for all of them.
+  // valid_lo[h] / valid_hi[h]: validity of rows row0+16h+g and row0+16h+g+8.
+  template <int N>
+  __device__ __forceinline__ void consume_rows(uint32_t kbase, uint32_t vbase, uint32_t region_bytes, int row0,
+                                               const bool (&valid_lo)[N], const bool (&valid_hi)[N], float scale_log2,
+                                               int lane) {
+    float s[N][4], s2[N][4];
+#pragma unroll
+    for (int h = 0; h < N; ++h)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[h][c] = s2[h][c] = 0.f;
+    {
+      const uint32_t hi = lane >> 4;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+        for (int h = 0; h < N; ++h) {
+          const uint32_t row = row0 + 16 * h + ((lane >> 3) & 1) * 8 + (lane & 7);
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4(kbase + (ks >> 2) * region_bytes + swz128(row, 2 * (ks & 3) + hi), a0, a1, a2, a3);
+          mma_16816((ks & 1) ? s2[h] : s[h], a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
+        }
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < N; ++h)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[h][c] += s2[h][c];
+    uint32_t pb[N][2];
+    softmax_rows<N>(s, valid_lo, valid_hi, scale_log2, pb);
+    const uint32_t mi = lane >> 3;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int h = 0; h < N; ++h) {
+        const uint32_t row = row0 + 16 * h + (mi >> 1) * 8 + (lane & 7);
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4_trans(vbase + (j >> 2) * region_bytes + swz128(row, 2 * (j & 3) + (mi & 1)), a0, a1, a2, a3);
+        mma_16816(acc[j], a0, a1, a2, a3, pb[h][0], pb[h][1]);
+      }
+    }
+  }
 };
 
 // Cross-warp merge buffers for the epilogue of one (unit, token-range) piece.

@@ -89,6 +89,10 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
   }
 }
 
+// Order this thread's generic-proxy shared-memory writes before later
+// async-proxy (TMA) accesses of the same buffer.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // ---------------------------------------------------------------- TMA
 // Tiled tensor loads into this CTA's shared memory, completion counted in
 // bytes on an mbarrier.  Plain (non-multicast) form only.

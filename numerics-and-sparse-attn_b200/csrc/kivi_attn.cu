@@ -21,9 +21,11 @@
 // batch 0, residual) are issued before that length is read.  Q-batches after
 // the first that hold no attended token are skipped by every warp alike.
 //
-// Warp 4 issues the loads; warps 0-3 consume, taking jobs (a quantized group,
-// or 16 rows of an F-tile) by a static cost-balanced assignment that every warp
-// computes alike.  A quantized group is dequantized in
+// Warps 0-3 consume, taking jobs (a quantized group, or 16 rows of an F-tile)
+// by a static cost-balanced assignment that every warp computes alike; lane 0
+// of warp 0 also issues the loads.  With no separate producer warp, a CTA is 4
+// warps and two CTAs per SM leave up to 255 registers per thread, which the
+// dequantization's independent chains need to overlap.  A quantized group is dequantized in
 // registers straight into mma.sync fragments, with no shared-memory round trip:
 //   K  S^T = (C - Z) (s*Q)^T: the per-channel scale s is folded into the query
 //      once per group; C (2-bit codes as exact fp16 integers, made with the
@@ -43,13 +45,13 @@
 
 #include "attn_engine.cuh"
 #include "host_util.h"
+#include "quant_math.cuh"
 
 namespace nsa {
 namespace {
 
-constexpr int kCWarps = 4;                 // consumer warps
-constexpr int kProducerWarp = kCWarps;
-constexpr int kThreads = (kCWarps + 1) * 32;
+constexpr int kCWarps = 4;                 // consumer warps (warp 0, lane 0 also issues the loads)
+constexpr int kThreads = kCWarps * 32;
 constexpr int kCtasPerSm = 2;
 constexpr int kFRows = 80;                 // residual slots per F-tile
 constexpr uint32_t kFRegion = kFRows * 128;  // 80 rows x 64 dims fp16
@@ -104,7 +106,7 @@ struct KParams {
   int n_kv_heads;
   int layout;  // 0: reference 14-tensor layout; 1: streaming ring
   int64_t seq_len;
-  const int64_t* unit_lens;
+  int64_t* unit_lens;
   int window, sink, residual, n_groups, res_cap;
   int n_qb, n_ft, items;  // items per unit: Q-batch 0, n_ft F-tiles, Q-batches 1 .. n_qb-1
   int ppu;                // pieces (CTAs) per unit
@@ -125,6 +127,14 @@ struct KParams {
   float* part_lse;
   float* part_o;
   int* err;
+  // fused quantize-on-append (stream layout, one CTA per unit); new_k == null:
+  // attention only.  The cache arrays above are then also written.
+  const __half* new_k;
+  const __half* new_v;
+  __half* k_res;
+  __half* v_res;
+  __half* sink_k16;
+  __half* sink_v16;
 };
 
 __device__ __forceinline__ int32_t clampi(int64_t x, int64_t lo, int64_t hi) {
@@ -132,8 +142,9 @@ __device__ __forceinline__ int32_t clampi(int64_t x, int64_t lo, int64_t hi) {
 }
 
 // Per-unit metadata from the unit's length (see nsa_kivi_stream_cache and
-// _kv_indices, sparse_kernel.py:15-46, for the two layouts).
-__device__ __forceinline__ KiviMeta make_meta(const KParams& p, int64_t unit) {
+// _kv_indices, sparse_kernel.py:15-46, for the two layouts); `len` is the
+// streaming unit's length (unused for the reference layout).
+__device__ __forceinline__ KiviMeta make_meta(const KParams& p, int64_t len_stream) {
   KiviMeta m;
   const int64_t S = p.sink, W = p.window, R = p.residual, NG = p.n_groups;
   if (p.layout == 0) {
@@ -148,7 +159,7 @@ __device__ __forceinline__ KiviMeta make_meta(const KParams& p, int64_t unit) {
     m.n_res = static_cast<int32_t>(R);
     m.res_skip = clampi(n_inv - nw, 0, R);
   } else {
-    const int64_t len = p.unit_lens[unit];
+    const int64_t len = len_stream;
     const int64_t C = p.res_cap;
     const int64_t n_stream = len > S ? len - S : 0;
     const int64_t F = n_stream > R ? (n_stream - R) / 32 : 0;  // flushed groups
@@ -428,10 +439,242 @@ __device__ __forceinline__ void zero_invalid_v_rows(uint32_t vbase, uint32_t reg
       asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(a), "r"(0u));
     }
   }
+  fence_proxy_async_smem();  // the stage is refilled by TMA later
   __syncwarp();
 }
 
 __device__ __forceinline__ void cwarps_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory"); }
+
+// ------------------------------------------------------- fused append
+// Quantize-on-append inside the decode launch (stream layout, one CTA per
+// unit): the same bit-exact arithmetic and cache layout as kivi_append_kernel
+// in kivi_quant.cu, which it replaces for such launches.  Its results also go
+// into the staged copies this launch attends over.
+__device__ __forceinline__ void sts8(uint32_t a, uint32_t v) { asm volatile("st.shared.u8 [%0], %1;" ::"r"(a), "r"(v)); }
+__device__ __forceinline__ void sts16(uint32_t a, __half v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "h"(__half_as_ushort(v)));
+}
+__device__ __forceinline__ void sts64(uint32_t a, uint32_t x, uint32_t y) {
+  asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(a), "r"(x), "r"(y));
+}
+
+struct AppendPlan {
+  bool sink = false;    // the appended token is a sink token: the sink group is re-quantized
+  int f_item = -1;      // F-tile and row holding the appended token's residual slot (-1: none)
+  int f_row = 0;
+  int fl_batch = -1;    // Q-batch and batch slot of the window group this append flushes (-1: none)
+  int fl_slot = 0;
+  int fl_gs = 0;        // its window-group slot
+  int64_t fl_base = 0;  // stream index of its first token
+};
+
+// Store the new token (thread c: channel c) and plan the rest; pos = the
+// unit's length before the append.
+__device__ __forceinline__ AppendPlan append_begin(const KParams& p, int64_t unit, int64_t pos, __half kx, __half vx,
+                                                   int c) {
+  AppendPlan a;
+  const int S = p.sink, R = p.residual, C = p.res_cap, NG = p.n_groups;
+  if (pos < S) {
+    p.sink_k16[(unit * S + pos) * kHeadDim + c] = kx;  // read back after a CTA barrier
+    p.sink_v16[(unit * S + pos) * kHeadDim + c] = vx;
+    a.sink = true;
+    return a;
+  }
+  const int64_t i = pos - S;  // stream index
+  const int slot = static_cast<int>(i % C);
+  p.k_res[(unit * C + slot) * kHeadDim + c] = kx;
+  p.v_res[(unit * C + slot) * kHeadDim + c] = vx;
+  a.f_item = slot / kFRows;
+  a.f_row = slot % kFRows;
+  const int64_t f_old = (i - R) >= 0 ? (i - R) / 32 : 0;  // groups flushed before this token
+  const int64_t f_new = (i + 1 - R) >= 0 ? (i + 1 - R) / 32 : 0;
+  if (f_new > f_old && NG > 0) {  // stream group f_old leaves the residual
+    a.fl_gs = static_cast<int>(f_old % NG);
+    a.fl_base = 32 * f_old;
+    a.fl_batch = (a.fl_gs + 1) / kBatchGroups;
+    a.fl_slot = (a.fl_gs + 1) % kBatchGroups;
+  }
+  return a;
+}
+
+// Write the appended token into the staged F-tile at `row` (thread c: channel c).
+__device__ __forceinline__ void patch_residual_row(uint32_t sd, int row, __half kx, __half vx, int c) {
+  const uint32_t off = (c >> 6) * kFRegion + swz128(row, (c & 63) >> 3) + (c & 7) * 2;
+  sts16(sd + off, kx);
+  sts16(sd + kFTile + off, vx);
+  fence_proxy_async_smem();
+}
+
+// One group record (K of channel c, V of token c/4 x channel group c%4) from
+// the group's 32 K values of channel c and 32 V values of its token and
+// channel group: into Q-stage slot `sl` at `qs` and to the cache arrays.
+__device__ __forceinline__ void store_group_record(const float (&x)[32], const float (&y)[32], uint32_t qs, int sl,
+                                                   uint8_t* kp, __half* ks, __half* kz, uint8_t* vp, __half* vs,
+                                                   __half* vz, int c) {
+  float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    mn = fminf(mn, x[j]);
+    mx = fmaxf(mx, x[j]);
+  }
+  GroupParams gp = group_params(mn, mx);
+  const __half hs = __float2half_rn(gp.scale), hz = __float2half_rn(gp.zero);
+  ks[c] = hs;
+  kz[c] = hz;
+  sts16(qs + kOffKS + sl * 256 + c * 2, hs);
+  sts16(qs + kOffKZ + sl * 256 + c * 2, hz);
+#pragma unroll
+  for (int bq = 0; bq < 8; ++bq) {
+    uint32_t byte = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) byte |= code_of(x[4 * bq + j], gp) << (2 * j);
+    kp[bq * kHeadDim + c] = static_cast<uint8_t>(byte);
+    sts8(qs + kOffKP + sl * 1024 + bq * kHeadDim + c, byte);
+  }
+  const int tok = c >> 2, q = c & 3;
+  mn = INFINITY;
+  mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    mn = fminf(mn, y[j]);
+    mx = fmaxf(mx, y[j]);
+  }
+  gp = group_params(mn, mx);
+  const __half vhs = __float2half_rn(gp.scale), vhz = __float2half_rn(gp.zero);
+  vs[tok * 4 + q] = vhs;
+  vz[tok * 4 + q] = vhz;
+  sts16(qs + kOffVS + sl * 256 + (tok * 4 + q) * 2, vhs);
+  sts16(qs + kOffVZ + sl * 256 + (tok * 4 + q) * 2, vhz);
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) lo |= code_of(y[j], gp) << (2 * j);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) hi |= code_of(y[16 + j], gp) << (2 * j);
+  *reinterpret_cast<uint2*>(vp + tok * 32 + q * 8) = make_uint2(lo, hi);
+  sts64(qs + kOffVP + sl * 1024 + tok * 32 + q * 8, lo, hi);
+  fence_proxy_async_smem();
+}
+
+// The padded sink group of a unit holding n sink tokens (the n real ones,
+// then copies of token 0), into batch 0's slot 0 and the sink arrays.
+__device__ __forceinline__ void requantize_sink(const KParams& p, int64_t unit, int n, uint32_t qs, int c) {
+  const int S = p.sink;
+  float x[32], y[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) x[j] = __half2float(p.sink_k16[(unit * S + (j < n ? j : 0)) * kHeadDim + c]);
+  const int tok = c >> 2, q = c & 3;
+  const __half* vrow = p.sink_v16 + (unit * S + (tok < n ? tok : 0)) * kHeadDim + q * 32;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) y[j] = __half2float(vrow[j]);
+  store_group_record(x, y, qs, 0, const_cast<uint8_t*>(p.ks_p) + unit * 1024, const_cast<__half*>(p.ks_s) + unit * 128,
+                     const_cast<__half*>(p.ks_z) + unit * 128, const_cast<uint8_t*>(p.vs_p) + unit * 1024,
+                     const_cast<__half*>(p.vs_s) + unit * 128, const_cast<__half*>(p.vs_z) + unit * 128, c);
+}
+
+// Stream group [base, base + 32) leaving the residual ring: into Q-stage slot
+// `sl` and window-group slot gs.
+__device__ __forceinline__ void quantize_flushed_group(const KParams& p, int64_t unit, int64_t base, int gs,
+                                                       uint32_t qs, int sl, int c) {
+  const int C = p.res_cap;
+  float x[32], y[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) x[j] = __half2float(p.k_res[(unit * C + (base + j) % C) * kHeadDim + c]);
+  const int tok = c >> 2, q = c & 3;
+  const __half* vrow = p.v_res + (unit * C + (base + tok) % C) * kHeadDim + q * 32;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) y[j] = __half2float(vrow[j]);
+  const int64_t g = unit * p.n_groups + gs;
+  store_group_record(x, y, qs, sl, const_cast<uint8_t*>(p.kw_p) + g * 1024, const_cast<__half*>(p.kw_s) + g * 128,
+                     const_cast<__half*>(p.kw_z) + g * 128, const_cast<uint8_t*>(p.vw_p) + g * 1024,
+                     const_cast<__half*>(p.vw_s) + g * 128, const_cast<__half*>(p.vw_z) + g * 128, c);
+}
+
+// Load issue, run by lane 0 of warp 0.  Each ring is filled in order; an
+// item is issued once warp 0 itself has consumed the previous user of its
+// stage (the other warps' release is then waited for, which never depends on
+// an item not yet issued).
+struct Issuer {
+  const KParams& p;
+  Smem& sm;
+  const CUtensorMap* tmK;
+  const CUtensorMap* tmV;
+  int64_t unit;
+  int f_next, f_end, b_next, b_end;
+  uint32_t f_issued = 0, q_issued = 0;
+  bool ok = true;
+
+  __device__ __forceinline__ Issuer(const KParams& p_, Smem& sm_, const CUtensorMap* k, const CUtensorMap* v,
+                                    int64_t u, int f0, int f1, int b0, int b1)
+      : p(p_), sm(sm_), tmK(k), tmV(v), unit(u), f_next(f0), f_end(f1), b_next(b0), b_end(b1) {}
+
+  // Q-batch b into Q stage s: the sink group (batch 0) and window groups p0..p1-1.
+  __device__ __forceinline__ void batch(int b, uint32_t s) {
+    const uint32_t fb = smem_u32(&sm.q_full[s]);
+    const uint32_t sd = smem_u32(sm.qb[s]);
+    const int p0 = b == 0 ? 0 : kBatchGroups * b - 1;  // batch slot v holds group v - 1
+    const int p1 = min(p.n_groups, kBatchGroups * b + kBatchGroups - 1);
+    const int so = p0 + 1 - kBatchGroups * b;
+    const uint32_t ng = p1 > p0 ? p1 - p0 : 0;
+    mbar_arrive_expect_tx(fb, (b == 0 ? 3072u : 0u) + ng * 3072u);
+    if (ng) {
+      const int64_t gbase = unit * p.n_groups + p0;
+      bulk_load(sd + kOffKP + so * 1024, p.kw_p + gbase * 1024, ng * 1024, fb);
+      bulk_load(sd + kOffKS + so * 256, p.kw_s + gbase * 128, ng * 256, fb);
+      bulk_load(sd + kOffKZ + so * 256, p.kw_z + gbase * 128, ng * 256, fb);
+      bulk_load(sd + kOffVP + so * 1024, p.vw_p + gbase * 1024, ng * 1024, fb);
+      bulk_load(sd + kOffVS + so * 256, p.vw_s + gbase * 128, ng * 256, fb);
+      bulk_load(sd + kOffVZ + so * 256, p.vw_z + gbase * 128, ng * 256, fb);
+    }
+    if (b == 0) {
+      bulk_load(sd + kOffKP, p.ks_p + unit * 1024, 1024, fb);
+      bulk_load(sd + kOffKS, p.ks_s + unit * 128, 256, fb);
+      bulk_load(sd + kOffKZ, p.ks_z + unit * 128, 256, fb);
+      bulk_load(sd + kOffVP, p.vs_p + unit * 1024, 1024, fb);
+      bulk_load(sd + kOffVS, p.vs_s + unit * 128, 256, fb);
+      bulk_load(sd + kOffVZ, p.vs_z + unit * 128, 256, fb);
+    }
+  }
+  // Batch 0 (always live): the first use of Q stage 0.
+  __device__ __forceinline__ void batch0() {
+    batch(0, 0);
+    q_issued = 1;
+  }
+  // F-tiles, while warp 0 has consumed the previous user of the stage (f_cons F-tiles consumed).
+  __device__ __forceinline__ void pump_f(uint32_t f_cons) {
+    while (ok && f_next < f_end && f_issued < f_cons + kFStages) {
+      const uint32_t s = f_issued % kFStages, ph = (f_issued / kFStages) & 1;
+      if (!mbar_wait(smem_u32(&sm.f_empty[s]), ph ^ 1, p.err)) {
+        ok = false;
+        break;
+      }
+      const uint32_t fb = smem_u32(&sm.f_full[s]);
+      const uint32_t sd = smem_u32(sm.f[s]);
+      mbar_arrive_expect_tx(fb, kFStageBytes);
+      const int uu = static_cast<int>(unit);
+      tma_load_4d(sd, tmK, fb, 0, f_next * kFRows, 0, uu);
+      tma_load_4d(sd + kFTile, tmV, fb, 0, f_next * kFRows, 0, uu);
+      ++f_issued;
+      ++f_next;
+    }
+  }
+  // Live Q-batches after the first, likewise (q_cons Q-batches consumed).
+  __device__ __forceinline__ void pump_q(const KiviMeta& meta, uint32_t q_cons) {
+    while (ok && b_next < b_end && q_issued < q_cons + kQStages) {
+      if (!batch_live(p, meta, b_next)) {
+        ++b_next;
+        continue;
+      }
+      const uint32_t s = q_issued % kQStages, ph = (q_issued / kQStages) & 1;
+      if (!mbar_wait(smem_u32(&sm.q_empty[s]), ph ^ 1, p.err)) {
+        ok = false;
+        break;
+      }
+      batch(b_next, s);
+      ++q_issued;
+      ++b_next;
+    }
+  }
+};
 
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     kivi_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
@@ -467,79 +710,43 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   }
   __syncthreads();
 
-  if (warp == kProducerWarp) {
-    // ---------------------------------------------------------- producer
-    if (lane == 0) {
-      prefetch_tmap(&tmK);
-      prefetch_tmap(&tmV);
-      // Q-batch b into stage s: the sink group (batch 0) and window groups p0..p1-1
-      auto issue_batch = [&](int b, uint32_t s) {
-        const uint32_t fb = smem_u32(&sm.q_full[s]);
-        const uint32_t sd = smem_u32(sm.qb[s]);
-        const int p0 = b == 0 ? 0 : kBatchGroups * b - 1;  // batch slot v holds group v - 1
-        const int p1 = min(p.n_groups, kBatchGroups * b + kBatchGroups - 1);
-        const int so = p0 + 1 - kBatchGroups * b;
-        const uint32_t ng = p1 > p0 ? p1 - p0 : 0;
-        mbar_arrive_expect_tx(fb, (b == 0 ? 3072u : 0u) + ng * 3072u);
-        if (ng) {
-          const int64_t gbase = unit * p.n_groups + p0;
-          bulk_load(sd + kOffKP + so * 1024, p.kw_p + gbase * 1024, ng * 1024, fb);
-          bulk_load(sd + kOffKS + so * 256, p.kw_s + gbase * 128, ng * 256, fb);
-          bulk_load(sd + kOffKZ + so * 256, p.kw_z + gbase * 128, ng * 256, fb);
-          bulk_load(sd + kOffVP + so * 1024, p.vw_p + gbase * 1024, ng * 1024, fb);
-          bulk_load(sd + kOffVS + so * 256, p.vw_s + gbase * 128, ng * 256, fb);
-          bulk_load(sd + kOffVZ + so * 256, p.vw_z + gbase * 128, ng * 256, fb);
-        }
-        if (b == 0) {
-          bulk_load(sd + kOffKP, p.ks_p + unit * 1024, 1024, fb);
-          bulk_load(sd + kOffKS, p.ks_s + unit * 128, 256, fb);
-          bulk_load(sd + kOffKZ, p.ks_z + unit * 128, 256, fb);
-          bulk_load(sd + kOffVP, p.vs_p + unit * 1024, 1024, fb);
-          bulk_load(sd + kOffVS, p.vs_s + unit * 128, 256, fb);
-          bulk_load(sd + kOffVZ, p.vs_z + unit * 128, 256, fb);
-        }
-      };
-      uint32_t nq = 0;
-      if (has_b0) issue_batch(0, nq++);  // first use of stage 0: nothing to wait for
-      bool ok = true;
-      uint32_t nf = 0;
-      for (int f = f_begin; f < f_end && ok; ++f) {
-        const uint32_t s = nf % kFStages, ph = (nf / kFStages) & 1;
-        ++nf;
-        if (!mbar_wait(smem_u32(&sm.f_empty[s]), ph ^ 1, p.err)) { ok = false; break; }
-        const uint32_t fb = smem_u32(&sm.f_full[s]);
-        const uint32_t sd = smem_u32(sm.f[s]);
-        mbar_arrive_expect_tx(fb, kFStageBytes);
-        const int uu = static_cast<int>(unit);
-        tma_load_4d(sd, &tmK, fb, 0, f * kFRows, 0, uu);
-        tma_load_4d(sd + kFTile, &tmV, fb, 0, f * kFRows, 0, uu);
-      }
-      const KiviMeta meta = make_meta(p, unit);
-      for (int b = b_begin; b < b_end && ok; ++b) {
-        if (!batch_live(p, meta, b)) continue;
-        const uint32_t s = nq % kQStages, ph = (nq / kQStages) & 1;
-        ++nq;
-        if (!mbar_wait(smem_u32(&sm.q_empty[s]), ph ^ 1, p.err)) { ok = false; break; }
-        issue_batch(b, s);
-      }
-    }
-    return;
+  // ------------------------------------------------------------- prologue
+  // Global loads of every thread go out first (the query -- 16 bytes per
+  // thread -- and, when appending, the unit's length and the new token's
+  // channel); then lane 0 of warp 0 issues batch 0 and the F-tiles (they do
+  // not depend on the unit's length) and, once the length is known, the live
+  // Q-batches the ring holds.
+  const int ct = threadIdx.x;
+  const uint4 qv = __ldg(reinterpret_cast<const uint4*>(p.q + (unit * kGroupHeads + (ct >> 4)) * kHeadDim +
+                                                       (ct & 15) * 8));
+  const bool appending = p.new_k != nullptr;
+  int64_t len = p.layout == 0 ? p.seq_len : p.unit_lens[unit];
+  __half new_kc = __float2half_rn(0.f), new_vc = new_kc;
+  if (appending) {
+    new_kc = p.new_k[unit * kHeadDim + ct];
+    new_vc = p.new_v[unit * kHeadDim + ct];
   }
+  Issuer iss(p, sm, &tmK, &tmV, unit, f_begin, f_end, b_begin, b_end);
+  const bool leader = threadIdx.x == 0;
+  if (leader) {
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+    if (has_b0) iss.batch0();
+    iss.pump_f(0);
+  }
+  const AppendPlan ap = appending ? append_begin(p, unit, len, new_kc, new_vc, ct) : AppendPlan{};
+  if (appending) ++len;
+  const KiviMeta meta = make_meta(p, len);
+  if (leader) iss.pump_q(meta, 0);
+  sts128(smem_u32(&sm.qpad[ct >> 4][(ct & 15) * 8]), qv.x, qv.y, qv.z, qv.w);
+  cwarps_sync();
 
   // -------------------------------------------------------------- consumers
   // A timed-out wait sets `aborted`: the warp then stops waiting (the error
   // word is already set) but keeps its schedule of named barriers.
   const int g = lane >> 2, t = lane & 3;
-  const KiviMeta meta = make_meta(p, unit);
   const LaneQ lq(lane);
   bool aborted = false;
-  {
-    const int ct = threadIdx.x;  // 128 consumer threads bring 16 bytes of the query each
-    const int row = ct >> 4, col = (ct & 15) * 8;
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.q + (unit * kGroupHeads + row) * kHeadDim + col));
-    sts128(smem_u32(&sm.qpad[row][col]), v.x, v.y, v.z, v.w);
-    cwarps_sync();
-  }
   WarpAttn st;
   st.reset();
   const uint32_t qpad = smem_u32(sm.qpad);
@@ -553,20 +760,45 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     if (phase == 1) {
 #pragma unroll 1
       for (int f = f_begin; f < f_end; ++f) {
+        if (leader) {
+          iss.pump_f(nf);
+          iss.pump_q(meta, nq);
+        }
+        __syncwarp();
         const uint32_t s = nf % kFStages, ph = (nf / kFStages) & 1;
         ++nf;
         if (!aborted && !mbar_wait(smem_u32(&sm.f_full[s]), ph, p.err)) aborted = true;
         const uint32_t sd = smem_u32(sm.f[s]);
+        if (ap.f_item == f) {  // the appended token's slot: its staged row is stale
+          patch_residual_row(sd, ap.f_row, new_kc, new_vc, ct);
+          cwarps_sync();
+        }
+        // jobs of 32 rows (the last one 16): one softmax step per job
 #pragma unroll 1
-        for (int hf = 0; hf < kFRows / 16; ++hf) {
-          const int r0 = f * kFRows + 16 * hf;
-          const bool v_lo = res_slot_valid(p, meta, r0 + g);
-          const bool v_hi = res_slot_valid(p, meta, r0 + g + 8);
-          if (!__any_sync(0xffffffffu, v_lo || v_hi)) continue;
-          if (js.take(kCostF) != warp) continue;
-          zero_invalid_v_rows(sd + kFTile, kFRegion, 16 * hf, v_lo, v_hi, lane);
+        for (int r = 0; r < kFRows; r += 32) {
+          const int r0 = f * kFRows + r;
+          const bool two = r + 32 <= kFRows;
+          bool vl[2], vh[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            vl[h] = (h == 0 || two) && res_slot_valid(p, meta, r0 + 16 * h + g);
+            vh[h] = (h == 0 || two) && res_slot_valid(p, meta, r0 + 16 * h + g + 8);
+          }
+          const bool any0 = __any_sync(0xffffffffu, vl[0] || vh[0]);
+          const bool any1 = __any_sync(0xffffffffu, vl[1] || vh[1]);
+          if (!any0 && !any1) continue;
+          if (js.take(kCostF * ((any0 ? 1 : 0) + (any1 ? 1 : 0))) != warp) continue;
           st.load_q(qpad, lane, kQPadStride * 2);  // reloaded here: not held across the quantized path
-          st.consume16(sd, sd + kFTile, kFRegion, 16 * hf, v_lo, v_hi, p.scale_log2, lane);
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            if (h == 0 || two) zero_invalid_v_rows(sd + kFTile, kFRegion, r + 16 * h, vl[h], vh[h], lane);
+          if (two && any0 && any1) {
+            st.consume_rows<2>(sd, sd + kFTile, kFRegion, r, vl, vh, p.scale_log2, lane);
+          } else {
+            const int h = any0 ? 0 : 1;
+            const bool l1[1] = {vl[h]}, h1[1] = {vh[h]};
+            st.consume_rows<1>(sd, sd + kFTile, kFRegion, r + 16 * h, l1, h1, p.scale_log2, lane);
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&sm.f_empty[s]));
@@ -577,10 +809,23 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 #pragma unroll 1
     for (int b = lo; b < hi; ++b) {
       if (!batch_live(p, meta, b)) continue;
+      if (leader) {
+        iss.pump_f(nf);
+        iss.pump_q(meta, nq);
+      }
+      __syncwarp();
       const uint32_t s = nq % kQStages, ph = (nq / kQStages) & 1;
       ++nq;
       if (!aborted && !mbar_wait(smem_u32(&sm.q_full[s]), ph, p.err)) aborted = true;
       const uint32_t qs = smem_u32(sm.qb[s]);
+      if (ap.sink && b == 0) {  // the sink group changed: re-quantize it into slot 0 (and the cache)
+        requantize_sink(p, unit, static_cast<int>(len), qs, ct);
+        cwarps_sync();
+      }
+      if (ap.fl_batch == b) {  // a window group was flushed: quantize it into its slot (and the cache)
+        quantize_flushed_group(p, unit, ap.fl_base, ap.fl_gs, qs, ap.fl_slot, ct);
+        cwarps_sync();
+      }
 #pragma unroll 1
       for (int gs = 0; gs < kBatchGroups; ++gs) {
         const uint32_t mask = group_mask(p, meta, b, gs);
@@ -598,8 +843,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   cwarps_sync();
   warp_publish(st, sm.ep, warp, lane);
   cwarps_sync();
-  const int ct = threadIdx.x;  // 0..127
-  const int hh = ct >> 4, d0 = (ct & 15) * 8;
+  const int hh = ct >> 4, d0 = (ct & 15) * 8;  // this thread's head and 8 dims
   float o[8], lse;
   {
     float o4[4];
@@ -608,6 +852,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     merge_warps(sm.ep, hh, d0 + 4, o4, lse);
     for (int i = 0; i < 4; ++i) o[4 + i] = o4[i];
   }
+  if (appending && ct == 0) p.unit_lens[unit] = len;  // every thread read the old length at entry
   __half* out = p.o + unit * kGroupHeads * kHeadDim;
   if (p.ppu == 1) {
     const float a[4] = {o[0], o[1], o[2], o[3]}, b[4] = {o[4], o[5], o[6], o[7]};
@@ -819,15 +1064,11 @@ size_t nsa_kivi_stream_workspace_bytes(const nsa_kivi_stream_cache* c) {
   return ws_bytes(plan(c->batch * c->n_kv_heads, static_cast<int>(c->n_groups), static_cast<int>(c->residual + 32)));
 }
 
-int nsa_kivi_stream_decode(const nsa_kivi_stream_cache* cache, const void* q, void* o, float sm_scale,
-                           void* workspace, size_t workspace_bytes, nsa_stream_t stream) {
-  clear_error();
-  if (!cache) return fail(NSA_ERR_INVALID, "null cache");
-  const nsa_kivi_stream_cache& c = *cache;
-  int rc = kivi_check_stream_cache(c);
-  if (rc) return rc;
-  if (!all_aligned({q, o})) return fail(NSA_ERR_ALIGN, "q and o must be non-null and 16-byte aligned");
-  KParams p{};
+namespace {
+
+// Kernel parameters of a streaming-cache launch (attention only).
+void stream_params(const nsa_kivi_stream_cache& c, const void* q, void* o, float sm_scale, KParams& p) {
+  p = KParams{};
   p.q = static_cast<const __half*>(q);
   p.o = static_cast<__half*>(o);
   p.n_kv_heads = static_cast<int>(c.n_kv_heads);
@@ -851,8 +1092,63 @@ int nsa_kivi_stream_decode(const nsa_kivi_stream_cache* cache, const void* q, vo
   p.vw_p = static_cast<const uint8_t*>(c.v_win_packed);
   p.vw_s = static_cast<const __half*>(c.v_win_scale);
   p.vw_z = static_cast<const __half*>(c.v_win_zero);
-  const Plan s = plan(c.batch * c.n_kv_heads, static_cast<int>(c.n_groups), static_cast<int>(c.residual + 32));
-  return launch(p, s, c.k_res, c.v_res, workspace, workspace_bytes, stream);
+}
+
+// Whether a decode step may append inside the attention launch (NSA_FUSED_APPEND=0
+// turns it off, for comparison).
+bool fused_append_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("NSA_FUSED_APPEND");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+Plan stream_plan(const nsa_kivi_stream_cache& c) {
+  return plan(c.batch * c.n_kv_heads, static_cast<int>(c.n_groups), static_cast<int>(c.residual + 32));
+}
+
+}  // namespace
+
+int nsa_kivi_stream_decode(const nsa_kivi_stream_cache* cache, const void* q, void* o, float sm_scale,
+                           void* workspace, size_t workspace_bytes, nsa_stream_t stream) {
+  clear_error();
+  if (!cache) return fail(NSA_ERR_INVALID, "null cache");
+  const nsa_kivi_stream_cache& c = *cache;
+  int rc = kivi_check_stream_cache(c);
+  if (rc) return rc;
+  if (!all_aligned({q, o})) return fail(NSA_ERR_ALIGN, "q and o must be non-null and 16-byte aligned");
+  KParams p;
+  stream_params(c, q, o, sm_scale, p);
+  return launch(p, stream_plan(c), c.k_res, c.v_res, workspace, workspace_bytes, stream);
+}
+
+int nsa_kivi_stream_decode_step(const nsa_kivi_stream_cache* cache, const void* new_k, const void* new_v,
+                                const void* q, void* o, float sm_scale, void* workspace, size_t workspace_bytes,
+                                nsa_stream_t stream) {
+  clear_error();
+  if (!cache || !new_k || !new_v) return fail(NSA_ERR_INVALID, "null pointer");
+  const nsa_kivi_stream_cache& c = *cache;
+  int rc = kivi_check_stream_cache(c);
+  if (rc) return rc;
+  if (!all_aligned({q, o, new_k, new_v}))
+    return fail(NSA_ERR_ALIGN, "q, o, new_k and new_v must be non-null and 16-byte aligned");
+  const Plan s = stream_plan(c);
+  if (s.ppu == 1 && fused_append_enabled()) {
+    KParams p;
+    stream_params(c, q, o, sm_scale, p);
+    p.new_k = static_cast<const __half*>(new_k);
+    p.new_v = static_cast<const __half*>(new_v);
+    p.k_res = static_cast<__half*>(c.k_res);
+    p.v_res = static_cast<__half*>(c.v_res);
+    p.sink_k16 = static_cast<__half*>(c.sink_k);
+    p.sink_v16 = static_cast<__half*>(c.sink_v);
+    return launch(p, s, c.k_res, c.v_res, workspace, workspace_bytes, stream);
+  }
+  // split units: append in its own launch, then attend
+  rc = nsa_kivi_append(cache, new_k, new_v, stream);
+  if (rc) return rc;
+  return nsa_kivi_stream_decode(cache, q, o, sm_scale, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

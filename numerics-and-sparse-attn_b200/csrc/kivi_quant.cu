@@ -14,6 +14,7 @@
 #include <cuda_fp16.h>
 
 #include "common.cuh"
+#include "quant_math.cuh"
 #include "host_util.h"
 
 namespace nsa {
@@ -26,22 +27,6 @@ __device__ __forceinline__ float ld_f32<float>(const float* p) { return *p; }
 template <>
 __device__ __forceinline__ float ld_f32<__half>(const __half* p) { return __half2float(*p); }
 
-struct GroupParams {
-  float scale, zero;
-};
-
-__device__ __forceinline__ GroupParams group_params(float mn, float mx) {
-  float scale = __fdiv_rn(__fsub_rn(mx, mn), 3.0f);
-  if (scale == 0.0f) scale = 1.0f;
-  const float zero = floorf(__fadd_rn(__fdiv_rn(-mn, scale), 0.5f));
-  return {scale, zero};
-}
-
-__device__ __forceinline__ uint32_t code_of(float x, const GroupParams& g) {
-  float q = __fadd_rn(floorf(__fadd_rn(__fdiv_rn(x, g.scale), 0.5f)), g.zero);
-  q = fminf(fmaxf(q, 0.0f), 3.0f);
-  return static_cast<uint32_t>(q);
-}
 
 // ---------------------------------------------------------------- K (per channel)
 // One thread per (unit, 32-token group, channel).  in: [U, T, D]; packed

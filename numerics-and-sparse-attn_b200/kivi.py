@@ -14,6 +14,7 @@ semantics are documented with ``nsa_kivi_stream_cache`` in include/nsa_b200.h.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
@@ -288,10 +289,34 @@ class KiviCache:
                                                           _lib.stream_handle(self.device)))
         return o
 
+    def step_launches(self) -> int:
+        """Kernel launches of one decode_step: 1 when every unit is decoded
+        by its own CTA (units > half the CTA slots, two per SM), else 2."""
+        if os.environ.get("NSA_FUSED_APPEND", "1").startswith("0"):
+            return 2
+        slots = 2 * torch.cuda.get_device_properties(self.device).multi_processor_count
+        units = self.batch * self.n_kv_heads
+        return 1 if units >= slots or 2 * units > slots else 2
+
     def decode_step(self, q, new_k, new_v, sm_scale=None):
-        """One decode step: quantize-on-append of the new token, then attend."""
-        self.append(new_k, new_v)
-        return self.attend(q, sm_scale)
+        """One decode step: quantize-on-append of the new token, then attend
+        (one launch when every unit gets its own CTA, else append + attend)."""
+        shape = (self.batch, self.n_kv_heads, self.head_dim)
+        for name, t in (("new_k", new_k), ("new_v", new_v)):
+            _req(isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == torch.float16 and t.is_contiguous()
+                 and tuple(t.shape) == shape, f"{name} must be a contiguous float16 CUDA tensor of shape {shape}")
+        _req(isinstance(q, torch.Tensor) and q.is_cuda and q.dtype == torch.float16 and q.is_contiguous()
+             and tuple(q.shape) == (self.batch, 8 * self.n_kv_heads, self.head_dim),
+             "q must be a contiguous float16 CUDA tensor [B, 8*Hkv, 128]")
+        if sm_scale is None:
+            sm_scale = self.head_dim ** -0.5
+        o = torch.empty_like(q)
+        with torch.cuda.device(self.device):
+            ws = _lib.workspace(self.device, self._ws_bytes)
+            _lib.check(_lib.load().nsa_kivi_stream_decode_step(
+                ctypes.byref(self._desc), new_k.data_ptr(), new_v.data_ptr(), q.data_ptr(), o.data_ptr(),
+                float(sm_scale), ws.data_ptr(), ws.numel(), _lib.stream_handle(self.device)))
+        return o
 
     # ---------------------------------------------------------------- filling
     def load_state(self, seq_len, sink_k, sink_v, tail_k=None, tail_v=None, tail_start=None):

@@ -256,6 +256,34 @@ def test_stream_full_size_synthetic_against_oracle():
             assert _err(o, ref) < TOL_2BIT, step
 
 
+@pytest.mark.parametrize("W", [256, 128])
+def test_fused_step_equals_append_then_attend(W):
+    """B=32 (every unit gets its own CTA): the one-launch decode step --
+    store, group flush or sink re-quantization and attention in the decode
+    kernel -- gives outputs and cache state bit-identical to nsa_kivi_append
+    followed by nsa_kivi_stream_decode, from an empty cache through the sink
+    phase, the first flushes (dropped groups when W == R) and eviction."""
+    B, Hkv, S, R = 32, 8, 4, 128
+    n_steps = S + max(W, R + 32) + R + 2 * 32 + 3
+    g = torch.Generator(device=DEV).manual_seed(70 + W)
+    fused = quant_kernel.KiviCache(B, Hkv, W, sink=S, residual=R, device=DEV)
+    split = quant_kernel.KiviCache(B, Hkv, W, sink=S, residual=R, device=DEV)
+    assert fused.step_launches() == 1
+    check_at = {1, 2, S, S + 1, S + R + 31, S + R + 32, S + R + 33, n_steps}
+    for L in range(1, n_steps + 1):
+        q = torch.randn(B, 64, 128, device=DEV, generator=g).half()
+        nk = (torch.randn(B, Hkv, 128, device=DEV, generator=g) * (1 + (L % 3))).half()
+        nv = torch.randn(B, Hkv, 128, device=DEV, generator=g).half()
+        o_f = fused.decode_step(q, nk, nv)
+        split.append(nk, nv)
+        o_s = split.attend(q)
+        assert torch.equal(o_f, o_s), L
+        if L in check_at:
+            a, b = _state_np(fused), _state_np(split)
+            for key in a:
+                np.testing.assert_array_equal(a[key], b[key], err_msg=f"{key} at L={L}")
+
+
 def test_no_device_error_recorded():
     import importlib
     pkg = importlib.import_module("numerics-and-sparse-attn_b200")
