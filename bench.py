@@ -174,9 +174,10 @@ class Workload:
         return o
 
     def attention_only(self, i: int):
-        """The dominant kernel alone (for the roofline): the attention launch."""
+        """The dominant kernel alone (for the roofline): the attention launch
+        (for kivi with a one-launch step, that launch: append + attention)."""
         j = i % self.n_layers
-        if self.name == "kivi":
+        if self.name == "kivi" and self.launches_per_step != 1:
             return self.layers[j].attend(self.q[j])
         return self.step(i)
 
@@ -393,7 +394,10 @@ def main():
                        % (wlobj.n_layers, wlobj.n_layers * bytes_step / 1e6)),
         "hbm_tbs_step": bytes_step / (step_ms * 1e-3) / 1e12,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "kernel": "attention" if name == "kivi" else name,
+                     "traffic": None,
+                     "kernel": ("kivi_decode_kernel (quantize-on-append + attention, one launch)"
+                                if wlobj.launches_per_step == 1 else "kivi_decode_kernel (attention)")
+                     if name == "kivi" else "fp16_decode_kernel",
                      "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
                      else "fallback 6.65 TB/s", "kernel_us": attn_ms * 1e3,
                      "algorithmic_bytes_per_launch": bytes_step},

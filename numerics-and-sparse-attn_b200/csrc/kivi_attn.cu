@@ -86,6 +86,7 @@ struct Smem {
   };
   uint8_t qb[kQStages][kQStageBytes];
   __half qpad[kGroupHeads][kQPadStride];  // the unit's query, rows padded: conflict-free fragment loads
+  __half newtok[2][kHeadDim];             // appended token's K and V (fused append)
   uint64_t f_full[kFStages], f_empty[kFStages];
   uint64_t q_full[kQStages], q_empty[kQStages];
 };
@@ -290,9 +291,15 @@ struct LaneQ {
   }
 };
 
+// Channels of lane t (t = lane % 4) on the K side: [16t, 16t+16) and
+// [64+16t, 64+16t+16); 16-byte chunk i (8 channels) of them starts at byte
+// chunk_off(i) + 32t of a channel-major fp16 row (codes: + 16t of a byte row).
+// This spreads the four t's over distinct banks for every load.
+__device__ __forceinline__ uint32_t chunk_off(int i) { return (i >> 1) * 128 + (i & 1) * 16; }
+
 // Attend to the attended tokens (`mask`) of the quantized group in batch slot
-// `gs` of the Q stage at `qs`.  qrow: this lane's query words Q[head g][32t ..
-// 32t+31] in shared memory (natural order).
+// `gs` of the Q stage at `qs`.  qrow: this lane's query row Q[head g] + 32t
+// bytes in shared memory (chunks at chunk_off).
 __device__ __forceinline__ void attend_group(WarpAttn& st, uint32_t qrow, const LaneQ& lq, uint32_t qs, int gs,
                                              uint32_t mask, float scale_log2, int lane) {
   const int g = lane >> 2, t = lane & 3;
@@ -304,18 +311,19 @@ __device__ __forceinline__ void attend_group(WarpAttn& st, uint32_t qrow, const 
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       uint32_t s0, s1, s2, s3, q0, q1, q2, q3;
-      lds128(qs + kOffKS + gs * 256 + 64 * t + 16 * i, s0, s1, s2, s3);
-      lds128(qrow + 16 * i, q0, q1, q2, q3);
+      lds128(qs + kOffKS + gs * 256 + 32 * t + chunk_off(i), s0, s1, s2, s3);
+      lds128(qrow + chunk_off(i), q0, q1, q2, q3);
       sq[4 * i] = hmul2u(q0, s0);
       sq[4 * i + 1] = hmul2u(q1, s1);
       sq[4 * i + 2] = hmul2u(q2, s2);
       sq[4 * i + 3] = hmul2u(q3, s3);
-      lds128(qs + kOffKZ + gs * 256 + 64 * t + 16 * i, zn[4 * i], zn[4 * i + 1], zn[4 * i + 2], zn[4 * i + 3]);
+      lds128(qs + kOffKZ + gs * 256 + 32 * t + chunk_off(i), zn[4 * i], zn[4 * i + 1], zn[4 * i + 2],
+             zn[4 * i + 3]);
     }
     float zc[4] = {0.f, 0.f, 0.f, 0.f}, zc2[4] = {0.f, 0.f, 0.f, 0.f};  // two chains: half the mma latency
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
-      // natural k order: k-cols (2t, 2t+1) = channels 32t+4kk+{0,1}, (2t+8, 2t+9) = +{2,3}
+      // natural k order: k-cols (2t, 2t+1) = the lane's channels 4kk+{0,1}, (2t+8, 2t+9) = +{2,3}
       mma_16816((kk & 1) ? zc2 : zc, zn[2 * kk], zn[2 * kk], zn[2 * kk + 1], zn[2 * kk + 1], sq[2 * kk],
                 sq[2 * kk + 1]);
       // permuted k order of the code fragments: (2t, 2t+1) = +{0,2}, (2t+8, 2t+9) = +{1,3}
@@ -337,15 +345,15 @@ __device__ __forceinline__ void attend_group(WarpAttn& st, uint32_t qrow, const 
       s[hf][0] = s[hf][2] = -zb0;
       s[hf][1] = s[hf][3] = -zb1;
       s2[hf][0] = s2[hf][1] = s2[hf][2] = s2[hf][3] = 0.f;
-      const uint32_t src = qs + kOffKP + gs * 1024 + (4 * hf + (g >> 1)) * 128 + 32 * t;
+      const uint32_t src = qs + kOffKP + gs * 1024 + (4 * hf + (g >> 1)) * 128 + 16 * t;
       lds128(src, kw[hf][0], kw[hf][1], kw[hf][2], kw[hf][3]);
-      lds128(src + 16, kw[hf][4], kw[hf][5], kw[hf][6], kw[hf][7]);
+      lds128(src + 64, kw[hf][4], kw[hf][5], kw[hf][6], kw[hf][7]);
     }
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        const uint32_t w = kw[hf][kk], wh = w >> 8;  // bytes: channels 32t+4kk+{0,1,2,3}
+        const uint32_t w = kw[hf][kk], wh = w >> 8;  // bytes: the lane's channels 4kk+{0,1,2,3}
         const uint32_t a0 = hsub2u((w & lq.mk_lo) | lq.mg_lo, lq.mg_lo);
         const uint32_t a1 = hsub2u((w & lq.mk_hi) | lq.mg_hi, lq.mg_hi);
         const uint32_t a2 = hsub2u((wh & lq.mk_lo) | lq.mg_lo, lq.mg_lo);
@@ -466,24 +474,22 @@ struct AppendPlan {
   int fl_slot = 0;
   int fl_gs = 0;        // its window-group slot
   int64_t fl_base = 0;  // stream index of its first token
+  int fl_s0 = -1;       // its first residual slot (-1: no flush)
+  __device__ __forceinline__ bool flushing(int slot) const { return fl_s0 >= 0 && slot >= fl_s0 && slot < fl_s0 + 32; }
 };
 
-// Store the new token (thread c: channel c) and plan the rest; pos = the
-// unit's length before the append.
-__device__ __forceinline__ AppendPlan append_begin(const KParams& p, int64_t unit, int64_t pos, __half kx, __half vx,
-                                                   int c) {
+// Where the append lands; pos = the unit's length before the append.  (The
+// token's own stores wait until its value is needed, so that no thread
+// stalls on its load early in the launch.)
+__device__ __forceinline__ AppendPlan append_plan(const KParams& p, int64_t pos) {
   AppendPlan a;
   const int S = p.sink, R = p.residual, C = p.res_cap, NG = p.n_groups;
   if (pos < S) {
-    p.sink_k16[(unit * S + pos) * kHeadDim + c] = kx;  // read back after a CTA barrier
-    p.sink_v16[(unit * S + pos) * kHeadDim + c] = vx;
     a.sink = true;
     return a;
   }
   const int64_t i = pos - S;  // stream index
   const int slot = static_cast<int>(i % C);
-  p.k_res[(unit * C + slot) * kHeadDim + c] = kx;
-  p.v_res[(unit * C + slot) * kHeadDim + c] = vx;
   a.f_item = slot / kFRows;
   a.f_row = slot % kFRows;
   const int64_t f_old = (i - R) >= 0 ? (i - R) / 32 : 0;  // groups flushed before this token
@@ -493,16 +499,20 @@ __device__ __forceinline__ AppendPlan append_begin(const KParams& p, int64_t uni
     a.fl_base = 32 * f_old;
     a.fl_batch = (a.fl_gs + 1) / kBatchGroups;
     a.fl_slot = (a.fl_gs + 1) % kBatchGroups;
+    a.fl_s0 = static_cast<int>(a.fl_base % C);
   }
   return a;
 }
 
-// Write the appended token into the staged F-tile at `row` (thread c: channel c).
-__device__ __forceinline__ void patch_residual_row(uint32_t sd, int row, __half kx, __half vx, int c) {
-  const uint32_t off = (c >> 6) * kFRegion + swz128(row, (c & 63) >> 3) + (c & 7) * 2;
-  sts16(sd + off, kx);
-  sts16(sd + kFTile + off, vx);
+// Copy the appended token (K and V rows of `tok`) into the staged F-tile at
+// `row`, by one warp: lane l moves 16 bytes (8 channels) of K (l < 16) or V.
+__device__ __forceinline__ void patch_residual_row(uint32_t sd, int row, uint32_t tok, int lane) {
+  const int kv = lane >> 4, chunk = lane & 15;  // chunk: 8 channels
+  uint32_t x, y, z, w;
+  lds128(tok + kv * kHeadDim * 2 + chunk * 16, x, y, z, w);
+  sts128(sd + kv * kFTile + (chunk >> 3) * kFRegion + swz128(row, chunk & 7), x, y, z, w);
   fence_proxy_async_smem();
+  __syncwarp();
 }
 
 // One group record (K of channel c, V of token c/4 x channel group c%4) from
@@ -571,18 +581,56 @@ __device__ __forceinline__ void requantize_sink(const KParams& p, int64_t unit, 
                      const_cast<__half*>(p.vs_s) + unit * 128, const_cast<__half*>(p.vs_z) + unit * 128, c);
 }
 
-// Stream group [base, base + 32) leaving the residual ring: into Q-stage slot
-// `sl` and window-group slot gs.
+// Stream group [base, base + 32) leaving the residual ring (slots s0 .. s0+31,
+// never wrapping: 32 divides both base and the ring size): into Q-stage slot
+// `sl` and window-group slot gs.  Read from the staged F-tiles when every
+// F-tile of the unit is still resident (f_stage0: the F ring's base address),
+// else from the cache.
 __device__ __forceinline__ void quantize_flushed_group(const KParams& p, int64_t unit, int64_t base, int gs,
-                                                       uint32_t qs, int sl, int c) {
+                                                       uint32_t qs, int sl, uint32_t f_stage0, int c) {
   const int C = p.res_cap;
-  float x[32], y[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) x[j] = __half2float(p.k_res[(unit * C + (base + j) % C) * kHeadDim + c]);
+  const int s0 = static_cast<int>(base % C);
   const int tok = c >> 2, q = c & 3;
-  const __half* vrow = p.v_res + (unit * C + (base + tok) % C) * kHeadDim + q * 32;
+  float x[32], y[32];
+  if (f_stage0) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) y[j] = __half2float(vrow[j]);
+    for (int j = 0; j < 32; ++j) {
+      const int slot = s0 + j, f = slot / kFRows, r = slot % kFRows;
+      const uint32_t a = f_stage0 + f * kFStageBytes + (c >> 6) * kFRegion + swz128(r, (c & 63) >> 3) + (c & 7) * 2;
+      unsigned short h;
+      asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(a));
+      x[j] = __half2float(__ushort_as_half(h));
+    }
+    const int slot = s0 + tok, f = slot / kFRows, r = slot % kFRows;
+    const uint32_t vb = f_stage0 + f * kFStageBytes + kFTile + (q >> 1) * kFRegion;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {  // channels q*32 + 8k .. +7
+      uint32_t w[4];
+      lds128(vb + swz128(r, (q & 1) * 4 + k), w[0], w[1], w[2], w[3]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f2 = __half22float2(u32_as_h2(w[e]));
+        y[8 * k + 2 * e] = f2.x;
+        y[8 * k + 2 * e + 1] = f2.y;
+      }
+    }
+  } else {
+    const __half* krow = p.k_res + (unit * C + s0) * kHeadDim + c;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = __half2float(krow[j * kHeadDim]);
+    const uint4* vrow = reinterpret_cast<const uint4*>(p.v_res + (unit * C + s0 + tok) * kHeadDim + q * 32);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint4 v = vrow[k];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f2 = __half22float2(u32_as_h2(w[e]));
+        y[8 * k + 2 * e] = f2.x;
+        y[8 * k + 2 * e + 1] = f2.y;
+      }
+    }
+  }
   const int64_t g = unit * p.n_groups + gs;
   store_group_record(x, y, qs, sl, const_cast<uint8_t*>(p.kw_p) + g * 1024, const_cast<__half*>(p.kw_s) + g * 128,
                      const_cast<__half*>(p.kw_z) + g * 128, const_cast<uint8_t*>(p.vw_p) + g * 1024,
@@ -734,11 +782,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     if (has_b0) iss.batch0();
     iss.pump_f(0);
   }
-  const AppendPlan ap = appending ? append_begin(p, unit, len, new_kc, new_vc, ct) : AppendPlan{};
+  const AppendPlan ap = appending ? append_plan(p, len) : AppendPlan{};
   if (appending) ++len;
   const KiviMeta meta = make_meta(p, len);
   if (leader) iss.pump_q(meta, 0);
   sts128(smem_u32(&sm.qpad[ct >> 4][(ct & 15) * 8]), qv.x, qv.y, qv.z, qv.w);
+  if (appending) {
+    sm.newtok[0][ct] = new_kc;
+    sm.newtok[1][ct] = new_vc;
+  }
   cwarps_sync();
 
   // -------------------------------------------------------------- consumers
@@ -750,13 +802,22 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   WarpAttn st;
   st.reset();
   const uint32_t qpad = smem_u32(sm.qpad);
-  const uint32_t qrow = qpad + g * (kQPadStride * 2) + 64 * t;
+  const uint32_t qrow = qpad + g * (kQPadStride * 2) + 32 * t;
   JobSched js;
   uint32_t nf = 0, nq = 0;
   // phase 0: Q-batch 0; phase 1: the F-tiles; phase 2: Q-batches b_begin ..
-  // (one loop so that each consumer path is instantiated once)
+  // (one loop so that each consumer path is instantiated once).  A group this
+  // launch flushes is quantized from the staged F-tiles after they have been
+  // consumed: when every item stays staged (resident), batch 0 keeps its place
+  // and only the flushed slot waits until after the F-tiles; otherwise the
+  // F-tiles come first and the group is read from the cache.
+  const bool flushing = ap.fl_batch >= 0;
+  const bool resident = p.n_qb <= kQStages && p.n_ft <= kFStages && f_begin == 0 && f_end == p.n_ft;
+  const bool defer_slot = flushing && resident && ap.fl_batch == 0;
+  const bool f_first = flushing && !resident;
 #pragma unroll 1
-  for (int phase = 0; phase < 3; ++phase) {
+  for (int step = 0; step < 3; ++step) {
+    const int phase = (f_first && step < 2) ? 1 - step : step;
     if (phase == 1) {
 #pragma unroll 1
       for (int f = f_begin; f < f_end; ++f) {
@@ -769,10 +830,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         ++nf;
         if (!aborted && !mbar_wait(smem_u32(&sm.f_full[s]), ph, p.err)) aborted = true;
         const uint32_t sd = smem_u32(sm.f[s]);
-        if (ap.f_item == f) {  // the appended token's slot: its staged row is stale
-          patch_residual_row(sd, ap.f_row, new_kc, new_vc, ct);
-          cwarps_sync();
-        }
         // jobs of 32 rows (the last one 16): one softmax step per job
 #pragma unroll 1
         for (int r = 0; r < kFRows; r += 32) {
@@ -788,10 +845,16 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           const bool any1 = __any_sync(0xffffffffu, vl[1] || vh[1]);
           if (!any0 && !any1) continue;
           if (js.take(kCostF * ((any0 ? 1 : 0) + (any1 ? 1 : 0))) != warp) continue;
+          if (ap.f_item == f && ap.f_row >= r && ap.f_row < r + (two ? 32 : 16))  // the appended token's
+            patch_residual_row(sd, ap.f_row, smem_u32(sm.newtok), lane);      // staged row is stale
           st.load_q(qpad, lane, kQPadStride * 2);  // reloaded here: not held across the quantized path
+          // V rows of unattended slots become 0 (P is 0 there, and 0 * NaN would not
+          // be), except those of a group this launch flushes: it is quantized from them
 #pragma unroll
           for (int h = 0; h < 2; ++h)
-            if (h == 0 || two) zero_invalid_v_rows(sd + kFTile, kFRegion, r + 16 * h, vl[h], vh[h], lane);
+            if (h == 0 || two)
+              zero_invalid_v_rows(sd + kFTile, kFRegion, r + 16 * h, vl[h] || ap.flushing(r0 + 16 * h + g),
+                                  vh[h] || ap.flushing(r0 + 16 * h + g + 8), lane);
           if (two && any0 && any1) {
             st.consume_rows<2>(sd, sd + kFTile, kFRegion, r, vl, vh, p.scale_log2, lane);
           } else {
@@ -802,6 +865,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&sm.f_empty[s]));
+      }
+      if (defer_slot) {  // batch 0 (stage 0) is still staged: its flushed slot now
+        const uint32_t qs = smem_u32(sm.qb[0]);
+        quantize_flushed_group(p, unit, ap.fl_base, ap.fl_gs, qs, ap.fl_slot, smem_u32(sm.f[0]), ct);
+        cwarps_sync();
+        const uint32_t mask = group_mask(p, meta, 0, ap.fl_slot);
+        const int halves = ((mask & 0xffffu) ? 1 : 0) + ((mask >> 16) ? 1 : 0);
+        if (mask && js.take(kCostGroup + kCostGroupHalf * halves) == warp)
+          attend_group(st, qrow, lq, qs, ap.fl_slot, mask, p.scale_log2, lane);
       }
       continue;
     }
@@ -819,17 +891,22 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       if (!aborted && !mbar_wait(smem_u32(&sm.q_full[s]), ph, p.err)) aborted = true;
       const uint32_t qs = smem_u32(sm.qb[s]);
       if (ap.sink && b == 0) {  // the sink group changed: re-quantize it into slot 0 (and the cache)
+        p.sink_k16[(unit * p.sink + len - 1) * kHeadDim + ct] = new_kc;  // fp16 copy of the new sink token
+        p.sink_v16[(unit * p.sink + len - 1) * kHeadDim + ct] = new_vc;
+        cwarps_sync();  // the copies are read back by other threads
         requantize_sink(p, unit, static_cast<int>(len), qs, ct);
         cwarps_sync();
       }
-      if (ap.fl_batch == b) {  // a window group was flushed: quantize it into its slot (and the cache)
-        quantize_flushed_group(p, unit, ap.fl_base, ap.fl_gs, qs, ap.fl_slot, ct);
+      if (ap.fl_batch == b && !defer_slot) {  // a window group was flushed: quantize it into its slot
+        // (and the cache); the F-tiles were consumed before, and are still staged when resident
+        quantize_flushed_group(p, unit, ap.fl_base, ap.fl_gs, qs, ap.fl_slot, resident ? smem_u32(sm.f[0]) : 0u,
+                               ct);
         cwarps_sync();
       }
 #pragma unroll 1
       for (int gs = 0; gs < kBatchGroups; ++gs) {
         const uint32_t mask = group_mask(p, meta, b, gs);
-        if (!mask) continue;
+        if (!mask || (defer_slot && b == 0 && gs == ap.fl_slot)) continue;
         const int halves = ((mask & 0xffffu) ? 1 : 0) + ((mask >> 16) ? 1 : 0);
         if (js.take(kCostGroup + kCostGroupHalf * halves) != warp) continue;
         attend_group(st, qrow, lq, qs, gs, mask, p.scale_log2, lane);
@@ -852,7 +929,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     merge_warps(sm.ep, hh, d0 + 4, o4, lse);
     for (int i = 0; i < 4; ++i) o[4 + i] = o4[i];
   }
-  if (appending && ct == 0) p.unit_lens[unit] = len;  // every thread read the old length at entry
+  if (appending) {
+    if (ap.f_item >= 0) {  // the new token's residual slot
+      const int64_t slot = (len - 1 - p.sink) % p.res_cap;
+      p.k_res[(unit * p.res_cap + slot) * kHeadDim + ct] = new_kc;
+      p.v_res[(unit * p.res_cap + slot) * kHeadDim + ct] = new_vc;
+    }
+    if (ct == 0) p.unit_lens[unit] = len;  // every thread read the old length at entry
+  }
   __half* out = p.o + unit * kGroupHeads * kHeadDim;
   if (p.ppu == 1) {
     const float a[4] = {o[0], o[1], o[2], o[3]}, b[4] = {o[4], o[5], o[6], o[7]};
