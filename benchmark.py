@@ -1,0 +1,173 @@
+"""W x L sweep of the three decode paths, with the reference's CSV columns.
+
+Drop-in for the reference's benchmark.py (benchmark.py:33-153): the same
+sweep (constants.CONTEXT_LENGTHS x constants.WINDOW_SIZES at BATCH=32, 64/8/128
+heads), the same public calls (dense_decode_attention, sparse_decode_attention,
+sparse_decode_attention_quantized over build_quantized_kv_cache), the same
+predicted-byte model and the same two CSV files with their columns, plus B200
+columns: achieved TB/s of each path from its predicted bytes and the fraction
+of the measured HBM peak (MEASURED_PEAKS.json, else 6.65 TB/s).
+
+Timing: each call is timed alone with CUDA events after an L2 flush (a write
+larger than the 126 MB L2), median over --reps calls after --warmup calls --
+the per-call methodology of the reference's triton.testing.do_bench, without
+Triton.  Dense K/V are allocated once per L and reused across W (the
+reference re-times the same dense call for every W).
+
+    python benchmark.py [--quick] [--reps N] [--out results]
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import json
+import os
+import statistics
+
+import torch
+
+from constants import (BATCH, CONTEXT_LENGTHS, D_HEAD, N_HEADS, N_KV_HEADS, RESIDUAL_SIZE, SINK_SIZE,
+                       WINDOW_SIZES)
+from dense_kernel import dense_decode_attention
+from quant_kernel import build_quantized_kv_cache, sparse_decode_attention_quantized
+from sparse_kernel import sparse_decode_attention
+
+B_FIXED_FP16 = 1_048_576  # Q + O bytes (benchmark.py:30 of the reference)
+C_FP16 = 131_072          # K + V bytes per cached token across the batch (benchmark.py:31)
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+
+def hbm_peak_tbs() -> float:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]) / 1e3
+    except Exception:
+        return 6.65
+
+
+class Timer:
+    """Median per-call device time (ms) with an L2 flush before every call."""
+
+    def __init__(self, reps: int, warmup: int):
+        self.reps, self.warmup = reps, warmup
+        self.flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        self.e0 = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+        self.e1 = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+
+    def __call__(self, fn) -> float:
+        for _ in range(self.warmup):
+            fn()
+        for i in range(self.reps):
+            self.flush.zero_()
+            self.e0[i].record()
+            fn()
+            self.e1[i].record()
+        torch.cuda.synchronize()
+        return statistics.median(a.elapsed_time(b) for a, b in zip(self.e0, self.e1))
+
+
+def randn(*shape, gen):
+    return torch.randn(*shape, generator=gen, device="cuda", dtype=torch.float32).half()
+
+
+def benchmark(lengths, windows, timer, peak):
+    """Native sparse vs dense, both fp16 (the reference's benchmark())."""
+    sm_scale = D_HEAD ** -0.5
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    results = []
+    for L in lengths:
+        q = randn(BATCH, N_HEADS, D_HEAD, gen=gen)
+        k_dense = randn(BATCH, N_KV_HEADS, L, D_HEAD, gen=gen)
+        v_dense = randn(BATCH, N_KV_HEADS, L, D_HEAD, gen=gen)
+        ms_dense = timer(lambda: dense_decode_attention(q, k_dense, v_dense, seq_len=L, sm_scale=sm_scale))
+        for W in windows:
+            k_cache = randn(BATCH, N_KV_HEADS, SINK_SIZE + W, D_HEAD, gen=gen)
+            v_cache = randn(BATCH, N_KV_HEADS, SINK_SIZE + W, D_HEAD, gen=gen)
+            ms_sparse = timer(lambda: sparse_decode_attention(q, k_cache, v_cache, seq_len=L, window=W))
+            bytes_sparse = B_FIXED_FP16 + C_FP16 * (W + SINK_SIZE)
+            bytes_dense = B_FIXED_FP16 + C_FP16 * L
+            predicted = bytes_dense / bytes_sparse
+            measured = ms_dense / ms_sparse
+            tbs_sparse, tbs_dense = bytes_sparse / ms_sparse / 1e9, bytes_dense / ms_dense / 1e9
+            results.append({
+                "L": L, "W": W, "ms_sparse": ms_sparse, "ms_dense": ms_dense,
+                "measured_ratio": measured, "predicted_ratio": predicted,
+                "gap_pct": 100 * (measured - predicted) / predicted,
+                "tbs_sparse": tbs_sparse, "tbs_dense": tbs_dense,
+                "frac_sparse": tbs_sparse / peak, "frac_dense": tbs_dense / peak,
+            })
+            del k_cache, v_cache
+        del k_dense, v_dense
+        torch.cuda.empty_cache()
+    return results
+
+
+def benchmark_quantized(lengths, windows, timer, peak):
+    """Quantized sparse vs native sparse vs dense (the reference's
+    benchmark_quantized()); W < RESIDUAL_SIZE is skipped as there."""
+    sm_scale = D_HEAD ** -0.5
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    keys = ["k_residual", "v_residual", "k_sink_packed", "k_sink_scale", "k_sink_zero", "v_sink_packed",
+            "v_sink_scale", "v_sink_zero", "k_win_packed", "k_win_scale", "k_win_zero", "v_win_packed",
+            "v_win_scale", "v_win_zero"]
+    results = []
+    for L in lengths:
+        q = randn(BATCH, N_HEADS, D_HEAD, gen=gen)
+        k_dense = randn(BATCH, N_KV_HEADS, L, D_HEAD, gen=gen)
+        v_dense = randn(BATCH, N_KV_HEADS, L, D_HEAD, gen=gen)
+        ms_dense = timer(lambda: dense_decode_attention(q, k_dense, v_dense, seq_len=L, sm_scale=sm_scale))
+        for W in [w for w in windows if w >= RESIDUAL_SIZE]:
+            kc = randn(BATCH, N_KV_HEADS, SINK_SIZE + W, D_HEAD, gen=gen)
+            vc = randn(BATCH, N_KV_HEADS, SINK_SIZE + W, D_HEAD, gen=gen)
+            ms_sparse = timer(lambda: sparse_decode_attention(q, kc, vc, seq_len=L, window=W))
+            cache = build_quantized_kv_cache(kc, vc)  # setup, not timed
+            args = [cache[k] for k in keys]
+            ms_quant = timer(lambda: sparse_decode_attention_quantized(q, *args, seq_len=L, window=W))
+            bytes_quant = sum(t.numel() * t.element_size() for t in args) + 2 * q.numel() * q.element_size()
+            bytes_sparse = B_FIXED_FP16 + C_FP16 * (W + SINK_SIZE)
+            predicted = bytes_sparse / bytes_quant
+            measured = ms_sparse / ms_quant
+            tbs_quant = bytes_quant / ms_quant / 1e9
+            results.append({
+                "L": L, "W": W, "ms_dense": ms_dense, "ms_sparse": ms_sparse, "ms_quantized": ms_quant,
+                "bytes_sparse_pred": bytes_sparse, "bytes_quantized_pred": bytes_quant,
+                "predicted_marginal_multiplier": predicted, "measured_marginal_multiplier": measured,
+                "gap_pct": 100 * (measured - predicted) / predicted,
+                "tbs_quantized": tbs_quant, "frac_quantized": tbs_quant / peak,
+            })
+            del kc, vc, cache, args
+        del k_dense, v_dense
+        torch.cuda.empty_cache()
+    return results
+
+
+def save(results, path):
+    header = list(results[0].keys())
+    print(" ".join(f"{h:>12}" for h in header))
+    for r in results:
+        print(" ".join(f"{v:>12.4f}" if isinstance(v, float) else f"{v:>12}" for v in r.values()))
+    with open(path, "w", newline="") as f:
+        writer = csv.DictWriter(f, fieldnames=header)
+        writer.writeheader()
+        writer.writerows(results)
+    print(f"\nSaved {len(results)} rows to {path}")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--quick", action="store_true", help="L in {8192, 163840}, W in {0, 128, 256, 4096}")
+    ap.add_argument("--reps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--out", default=os.path.join(ROOT, "results"))
+    a = ap.parse_args()
+    lengths, windows = CONTEXT_LENGTHS, WINDOW_SIZES
+    if a.quick:
+        lengths, windows = [8_192, 163_840], [0, 128, 256, 4096]
+    os.makedirs(a.out, exist_ok=True)
+    timer, peak = Timer(a.reps, a.warmup), hbm_peak_tbs()
+    save(benchmark(lengths, windows, timer, peak), os.path.join(a.out, "benchmark_results.csv"))
+    save(benchmark_quantized(lengths, windows, timer, peak), os.path.join(a.out, "benchmark_results_quantized.csv"))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,26 @@
+"""The W x L sweep (benchmark.py) runs and writes the reference's CSV columns
+(benchmark.py:65-71 and :140-147 of the reference), plus its B200 columns."""
+import pytest
+
+import benchmark
+
+pytestmark = pytest.mark.gpu
+
+REF_COLS = ["L", "W", "ms_sparse", "ms_dense", "measured_ratio", "predicted_ratio", "gap_pct"]
+REF_COLS_Q = ["L", "W", "ms_dense", "ms_sparse", "ms_quantized", "bytes_sparse_pred", "bytes_quantized_pred",
+              "predicted_marginal_multiplier", "measured_marginal_multiplier", "gap_pct"]
+
+
+def test_sweep_columns_and_byte_model(tmp_path):
+    timer = benchmark.Timer(reps=2, warmup=1)
+    rows = benchmark.benchmark([8192], [0, 256], timer, 6.45)
+    assert [r["W"] for r in rows] == [0, 256]
+    assert list(rows[0])[:len(REF_COLS)] == REF_COLS
+    assert all(r["ms_sparse"] > 0 and r["ms_dense"] > 0 for r in rows)
+    assert rows[1]["predicted_ratio"] == pytest.approx((1_048_576 + 131_072 * 8192) / (1_048_576 + 131_072 * 260))
+    rows_q = benchmark.benchmark_quantized([8192], [0, 256], timer, 6.45)
+    assert [r["W"] for r in rows_q] == [256]  # W < 128 is skipped, as in the reference
+    assert list(rows_q[0])[:len(REF_COLS_Q)] == REF_COLS_Q
+    assert rows_q[0]["bytes_quantized_pred"] == 21_757_952  # the csv's own W=256 figure
+    benchmark.save(rows_q, str(tmp_path / "q.csv"))
+    assert (tmp_path / "q.csv").read_text().splitlines()[0].startswith(",".join(REF_COLS_Q))
