@@ -293,6 +293,185 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 
+// ---------------------------------------------------------------------------
+// Short sink+window caches with at least one unit per SM: one CTA of 4 warps
+// per unit, two CTAs per SM, so that every unit's tiles are requested at
+// once.  The unit's S+W slots come in 96-slot tiles, K and V each as one TMA
+// box holding both 64-dim halves (2-stage ring: 192 slots in flight, the rest
+// as soon as the first tile is consumed); lane 0 of warp 0 issues them.  Warps
+// take 32-slot jobs round-robin and run the shared fp16 engine; the epilogue
+// merges the 4 warps (its buffers reuse the ring).
+namespace win {
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kRows = 96;
+constexpr int kStages = 2;
+constexpr uint32_t kRegion = kRows * 128;  // 96 slots x 64 dims fp16
+constexpr uint32_t kTile = 2 * kRegion;    // K (or V) of a tile
+constexpr uint32_t kStageB = 2 * kTile;    // 48 KiB
+constexpr int kQPad = kHeadDim + 8;        // 272-byte query rows: conflict-free ldmatrix
+constexpr int64_t kMaxSlots = 4 * kRows;   // longer caches use the persistent kernel
+struct Smem {
+  union {
+    uint8_t kv[kStages][kStageB];  // 1024-aligned TMA destinations
+    EpilogueSmem ep;               // after every tile has been consumed
+  };
+  __half qpad[kGroupHeads][kQPad];
+  uint64_t full[kStages], empty[kStages];
+};
+static_assert(offsetof(Smem, kv) == 0 && kStageB % 1024 == 0 && kRegion % 1024 == 0, "TMA tile destinations");
+static_assert(sizeof(EpilogueSmem) <= sizeof(uint8_t[kStages][kStageB]), "epilogue alias");
+constexpr size_t kSmem = sizeof(Smem);
+static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
+__device__ __forceinline__ void sync4() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
+}  // namespace win
+
+__global__ void __launch_bounds__(win::kThreads, 2)
+    window_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                         const Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  grid_launch_dependents();
+  grid_dependency_wait();  // the cache and q may come from the previous kernel of the stream
+  if (smem_u32(smem_raw) & 1023u) {  // TMA tile destinations need 1024-byte alignment
+    if (threadIdx.x == 0) set_error(p.err, NSA_ERR_ALIGN);
+    return;
+  }
+  win::Smem& sm = *reinterpret_cast<win::Smem*>(smem_raw);
+  const int ct = threadIdx.x, warp = ct >> 5, lane = ct & 31, g = lane >> 2;
+  const int64_t unit = blockIdx.x;
+  const int n_tiles = (p.sink + p.window + win::kRows - 1) / win::kRows;
+  if (ct == 0) {
+    for (int s = 0; s < win::kStages; ++s) {
+      mbar_init(smem_u32(&sm.full[s]), 1);
+      mbar_init(smem_u32(&sm.empty[s]), win::kWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  // Tile i uses stage i % kStages; it is issued once warp 0 itself has
+  // consumed tile i - kStages (the other warps' release is then waited for).
+  const bool leader = ct == 0;
+  int issued = 0;
+  bool issuing = true;
+  auto pump = [&](int consumed) {
+    while (issuing && issued < n_tiles && issued < consumed + win::kStages) {
+      const uint32_t s = issued % win::kStages, ph = (issued / win::kStages) & 1;
+      if (!mbar_wait(smem_u32(&sm.empty[s]), ph ^ 1, p.err)) {
+        issuing = false;
+        break;
+      }
+      const uint32_t fb = smem_u32(&sm.full[s]), sd = smem_u32(sm.kv[s]);
+      mbar_arrive_expect_tx(fb, win::kStageB);
+      tma_load_4d(sd, &tmK, fb, 0, issued * win::kRows, 0, static_cast<int>(unit));
+      tma_load_4d(sd + win::kTile, &tmV, fb, 0, issued * win::kRows, 0, static_cast<int>(unit));
+      ++issued;
+    }
+  };
+  const uint4 qv = __ldg(reinterpret_cast<const uint4*>(p.q + (unit * kGroupHeads + (ct >> 4)) * kHeadDim +
+                                                       (ct & 15) * 8));
+  if (leader) {
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+    pump(0);
+    // tiles beyond the ring go to L2 now, so that their refill waits on L2
+    for (int i = win::kStages; i < n_tiles; ++i) {
+      tma_prefetch_4d(&tmK, 0, i * win::kRows, 0, static_cast<int>(unit));
+      tma_prefetch_4d(&tmV, 0, i * win::kRows, 0, static_cast<int>(unit));
+    }
+  }
+  const PieceMeta meta = make_meta(p, unit);
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(smem_u32(&sm.qpad[ct >> 4][(ct & 15) * 8])),
+               "r"(qv.x), "r"(qv.y), "r"(qv.z), "r"(qv.w));
+  win::sync4();
+
+  WarpAttn st;
+  st.reset();
+  st.load_q(smem_u32(sm.qpad), lane, win::kQPad * 2);
+  bool aborted = false;
+  uint32_t job = 0;
+  for (int ti = 0; ti < n_tiles; ++ti) {
+    if (leader) pump(ti);
+    __syncwarp();
+    const uint32_t s = ti % win::kStages, ph = (ti / win::kStages) & 1;
+    if (!aborted && !mbar_wait(smem_u32(&sm.full[s]), ph, p.err)) aborted = true;
+    const uint32_t sd = smem_u32(sm.kv[s]);
+#pragma unroll 1
+    for (int r = 0; r < win::kRows; r += 32) {
+      const int64_t r0 = int64_t(ti) * win::kRows + r;
+      bool vl[2], vh[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        vl[h] = slot_valid(p, r0 + 16 * h + g, meta);
+        vh[h] = slot_valid(p, r0 + 16 * h + g + 8, meta);
+      }
+      const bool any0 = __any_sync(0xffffffffu, vl[0] || vh[0]);
+      const bool any1 = __any_sync(0xffffffffu, vl[1] || vh[1]);
+      if (!any0 && !any1) continue;
+      if ((job++ % win::kWarps) != static_cast<uint32_t>(warp)) continue;
+      if (any0 && any1) {
+        st.consume_rows<2>(sd, sd + win::kTile, win::kRegion, r, vl, vh, p.scale_log2, lane);
+      } else {
+        const int h = any0 ? 0 : 1;
+        const bool l1[1] = {vl[h]}, h1[1] = {vh[h]};
+        st.consume_rows<1>(sd, sd + win::kTile, win::kRegion, r + 16 * h, l1, h1, p.scale_log2, lane);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&sm.empty[s]));
+  }
+
+  // ---- epilogue: merge the 4 warps
+  win::sync4();
+  warp_publish(st, sm.ep, warp, lane);
+  win::sync4();
+  const int hh = ct >> 4, d0 = (ct & 15) * 8;  // this thread's head and 8 dims
+  float o4[4], lse;
+  __half* out = p.o + unit * kGroupHeads * kHeadDim + hh * kHeadDim + d0;
+  merge_warps(sm.ep, hh, d0, o4, lse);
+  store_half4(out, o4);
+  merge_warps(sm.ep, hh, d0 + 4, o4, lse);
+  store_half4(out + 4, o4);
+}
+
+// Whether a sink+window launch uses window_decode_kernel: short caches with
+// at least one unit per SM (NSA_SPARSE_KERNEL=persistent forces the other).
+bool use_window_kernel(int64_t n_units, int64_t slots) {
+  const char* env = getenv("NSA_SPARSE_KERNEL");
+  if (env && env[0] == 'p') return false;
+  const int sms = current_device().sm_count > 0 ? current_device().sm_count : 148;
+  return n_units >= sms && slots <= win::kMaxSlots && n_units <= 0x7fffffff;
+}
+
+int launch_window(Params& p, int64_t n_units, const void* k, const void* v, int64_t cap, cudaStream_t stream) {
+  if (n_units == 0) return NSA_OK;
+  p.n_units = n_units;
+  p.err = device_error_word();
+  if (!p.err) return fail(NSA_ERR_CUDA, "device error word unavailable");
+  // cache [units][cap][128] viewed as [units][2 halves][cap][64] (dims innermost first)
+  CUtensorMap mk, mv;
+  const uint64_t dims[4] = {64, static_cast<uint64_t>(cap), 2, static_cast<uint64_t>(n_units)};
+  const uint64_t strides[3] = {kHeadDim * 2, 128, static_cast<uint64_t>(cap) * kHeadDim * 2};
+  const uint32_t box[4] = {64, win::kRows, 2, 1};
+  int rc = encode_tiled(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, k, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_tiled(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  static bool attr_set[64] = {false};
+  const int dev = current_device().device;
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(window_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(win::kSmem));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    attr_set[dev] = true;
+  }
+  cudaError_t e = launch_kernel(window_decode_kernel, dim3(static_cast<unsigned>(n_units)), dim3(win::kThreads),
+                                win::kSmem, stream, mk, mv, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "window_decode_kernel launch");
+  return NSA_OK;
+}
+
 struct Split {
   int64_t n_units, tiles_per_unit, total_tiles;
   int n_ctas, max_pieces, unit_aligned;
@@ -356,6 +535,7 @@ int check_common(const void* q, const void* k, const void* v, const void* o, int
 int launch(Params& p, const Split& s, const void* k, const void* v, int64_t cap, void* ws, size_t ws_bytes,
            cudaStream_t stream) {
   if (s.n_units == 0) return NSA_OK;
+  if (p.mode == kSparse && use_window_kernel(s.n_units, cap)) return launch_window(p, s.n_units, k, v, cap, stream);
   if (cap > (int64_t(1) << 31) - kTile) return fail(NSA_ERR_UNSUPPORTED, "cache length too large for TMA coordinates");
   const size_t need = workspace_bytes(s);
   if (!ws || ws_bytes < need)

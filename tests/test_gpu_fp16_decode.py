@@ -125,10 +125,14 @@ def test_sparse_reference_cases_full_batch(L, W):
     assert _err(o2, ref) < TOL
 
 
-def test_sparse_ragged_per_sequence_lengths():
-    """Per-sequence seq_lens and ring heads: each row equals a B=1 call."""
-    B, W, S = 6, 256, 4
-    lens = [1, 3, 100, 260, 261, 5000]
+@pytest.mark.parametrize("B,W", [(6, 256), (30, 256), (24, 380), (20, 60)])
+def test_sparse_ragged_per_sequence_lengths(B, W):
+    """Per-sequence seq_lens and ring heads: each row equals a B=1 call
+    (B=6: the persistent kernel; B >= 19, i.e. >= 148 units: one CTA per unit,
+    with W + S = 260 / 384 / 64 slots in 3 / 4 / 1 tiles)."""
+    S = 4
+    lens = ([1, 3, 100, 260, 261, 5000] * 6)[:B]
+    lens = [L + (i // 6) * 7 for i, L in enumerate(lens)]
     q = torch.randn(B, 64, 128, device=DEV).half()
     k = torch.randn(B, 8, S + W, 128, device=DEV).half()
     v = torch.randn(B, 8, S + W, 128, device=DEV).half()
