@@ -91,6 +91,30 @@ int nsa_sparse_decode(const void* q, const void* k_cache, const void* v_cache, v
                       void* workspace, size_t workspace_bytes, nsa_stream_t stream);
 
 
+/* fp16 ring cache with per-unit lengths (no reference counterpart: the
+ * reference builds the compacted cache on the host,
+ * test_sparse_correctness.py:51-72).  Unit u = (b, kv_head) holds
+ * unit_lens[u] (int64 [B*Hkv], device) tokens: position p < sink at slot p,
+ * position p >= sink at slot sink + (p - sink) % window (dropped when window
+ * is 0), so its ring head is (len - sink) % window and the attended set is
+ * nsa_sparse_decode's.  nsa_ring_append stores one token per unit (new_k,
+ * new_v f16 [B, Hkv, D]) and advances unit_lens; nsa_ring_decode attends
+ * (workspace: nsa_sparse_workspace_bytes); nsa_ring_decode_step does both,
+ * in one launch when every unit has its own CTA (at least one unit per SM and
+ * sink + window <= 384), else as append + decode. */
+int nsa_ring_append(void* k_cache, void* v_cache, int64_t* unit_lens, const void* new_k, const void* new_v,
+                    int64_t batch, int64_t n_kv_heads, int64_t head_dim, int64_t window, int64_t sink,
+                    nsa_stream_t stream);
+int nsa_ring_decode(const void* q, const void* k_cache, const void* v_cache, void* o,
+                    int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+                    int64_t window, int64_t sink, const int64_t* unit_lens, float sm_scale,
+                    void* workspace, size_t workspace_bytes, nsa_stream_t stream);
+int nsa_ring_decode_step(const void* q, void* k_cache, void* v_cache, void* o,
+                         int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+                         int64_t window, int64_t sink, int64_t* unit_lens, const void* new_k,
+                         const void* new_v, float sm_scale, void* workspace, size_t workspace_bytes,
+                         nsa_stream_t stream);
+
 /* Same computation as nsa_sparse_decode, but allocates nothing and takes no
  * workspace.  No counterpart in the reference: it exists for callers that
  * cannot call cudaMalloc (or any allocator) where they decode, e.g. a host

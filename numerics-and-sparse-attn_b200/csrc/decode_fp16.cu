@@ -76,6 +76,16 @@ struct Params {
   float* part_lse;
   float* part_o;
   int* err;
+  // ring cache with per-unit lengths (sparse mode; null: seq_len / seq_lens /
+  // ring_heads): unit u holds unit_lens[u] tokens, position p >= sink at slot
+  // sink + (p - sink) % window, so its ring head is (len - sink) % window.
+  int64_t* unit_lens;
+  // one-launch append (window kernel only; null: attention only): the token
+  // new_k/new_v[u] is stored at position unit_lens[u] of k_w/v_w first.
+  const __half* new_k;
+  const __half* new_v;
+  __half* k_w;
+  __half* v_w;
 };
 
 // CTA owning global tile X under the even split of `total` tiles over `ctas`.
@@ -89,8 +99,13 @@ __device__ __forceinline__ int64_t unit_len(const Params& p, int64_t unit) {
 
 __device__ __forceinline__ PieceMeta make_meta(const Params& p, int64_t unit) {
   PieceMeta m;
-  m.len = unit_len(p, unit);
-  m.head = p.ring_heads ? p.ring_heads[unit / p.n_kv_heads] : 0;
+  if (p.unit_lens) {
+    m.len = p.unit_lens[unit] + (p.new_k ? 1 : 0);
+    m.head = (m.len > p.sink && p.window > 0) ? static_cast<int32_t>((m.len - p.sink) % p.window) : 0;
+  } else {
+    m.len = unit_len(p, unit);
+    m.head = p.ring_heads ? p.ring_heads[unit / p.n_kv_heads] : 0;
+  }
   // window slot with logical index i holds position len - W + i: valid iff >= S
   const int64_t n_inv = int64_t(p.sink) - (m.len - p.window);
   m.n_inv = static_cast<int32_t>(n_inv < 0 ? 0 : (n_inv > p.window ? p.window : n_inv));
@@ -113,7 +128,7 @@ __device__ __forceinline__ bool slot_valid(const Params& p, int64_t slot, const 
 
 // Number of tiles of `unit` that can hold a valid slot (dense: up to len).
 __device__ __forceinline__ int64_t unit_tiles(const Params& p, int64_t unit) {
-  if (p.mode == kDense) {
+  if (p.mode == kDense && !p.unit_lens) {
     const int64_t len = unit_len(p, unit);
     return min(p.tiles_per_unit, (len + kTile - 1) / kTile);
   }
@@ -317,6 +332,7 @@ struct Smem {
     EpilogueSmem ep;               // after every tile has been consumed
   };
   __half qpad[kGroupHeads][kQPad];
+  __half newtok[2][kHeadDim];  // appended token's K and V
   uint64_t full[kStages], empty[kStages];
 };
 static_assert(offsetof(Smem, kv) == 0 && kStageB % 1024 == 0 && kRegion % 1024 == 0, "TMA tile destinations");
@@ -370,6 +386,19 @@ __global__ void __launch_bounds__(win::kThreads, 2)
   };
   const uint4 qv = __ldg(reinterpret_cast<const uint4*>(p.q + (unit * kGroupHeads + (ct >> 4)) * kHeadDim +
                                                        (ct & 15) * 8));
+  // one-launch append: position pos = the unit's old length goes to slot
+  // `aslot` (tile aslot / kRows); the staged tile's row is patched by the warp
+  // whose job holds it, the cache slot and the length are stored at the end
+  const bool appending = p.new_k != nullptr;
+  int64_t pos = 0;
+  int aslot = -1;
+  if (appending) {
+    pos = p.unit_lens[unit];
+    aslot = pos < p.sink ? static_cast<int>(pos)
+                         : (p.window > 0 ? p.sink + static_cast<int>((pos - p.sink) % p.window) : -1);
+    sm.newtok[0][ct] = p.new_k[unit * kHeadDim + ct];
+    sm.newtok[1][ct] = p.new_v[unit * kHeadDim + ct];
+  }
   if (leader) {
     prefetch_tmap(&tmK);
     prefetch_tmap(&tmV);
@@ -409,6 +438,15 @@ __global__ void __launch_bounds__(win::kThreads, 2)
       const bool any1 = __any_sync(0xffffffffu, vl[1] || vh[1]);
       if (!any0 && !any1) continue;
       if ((job++ % win::kWarps) != static_cast<uint32_t>(warp)) continue;
+      if (aslot >= r0 && aslot < r0 + 32) {  // the appended token's staged row is stale
+        const int row = aslot - ti * win::kRows, kv = lane >> 4, chunk = lane & 15;
+        uint4 x = *reinterpret_cast<const uint4*>(&sm.newtok[kv][chunk * 8]);
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sd + kv * win::kTile + (chunk >> 3) * win::kRegion +
+                                                                    swz128(row, chunk & 7)),
+                     "r"(x.x), "r"(x.y), "r"(x.z), "r"(x.w));
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
       if (any0 && any1) {
         st.consume_rows<2>(sd, sd + win::kTile, win::kRegion, r, vl, vh, p.scale_log2, lane);
       } else {
@@ -432,6 +470,33 @@ __global__ void __launch_bounds__(win::kThreads, 2)
   store_half4(out, o4);
   merge_warps(sm.ep, hh, d0 + 4, o4, lse);
   store_half4(out + 4, o4);
+  if (appending) {  // every thread read the old length at entry
+    const int64_t cap = p.sink + p.window;
+    if (aslot >= 0) {
+      p.k_w[(unit * cap + aslot) * kHeadDim + ct] = sm.newtok[0][ct];
+      p.v_w[(unit * cap + aslot) * kHeadDim + ct] = sm.newtok[1][ct];
+    }
+    if (ct == 0) p.unit_lens[unit] = pos + 1;
+  }
+}
+
+// Append without attention (ring cache, any launch shape): one CTA of 128
+// threads (thread = channel) per unit stores the token and advances the length.
+__global__ void ring_append_kernel(__half* k, __half* v, int64_t* unit_lens, const __half* new_k, const __half* new_v,
+                                   int sink, int window) {
+  grid_launch_dependents();
+  grid_dependency_wait();  // the previous kernel may still read this cache
+  const int64_t u = blockIdx.x;
+  const int c = threadIdx.x;
+  const int64_t pos = unit_lens[u];
+  const int64_t cap = sink + window;
+  const int64_t slot = pos < sink ? pos : (window > 0 ? sink + (pos - sink) % window : -1);
+  if (slot >= 0) {
+    k[(u * cap + slot) * kHeadDim + c] = new_k[u * kHeadDim + c];
+    v[(u * cap + slot) * kHeadDim + c] = new_v[u * kHeadDim + c];
+  }
+  __syncthreads();  // every thread has read the length
+  if (c == 0) unit_lens[u] = pos + 1;
 }
 
 // Whether a sink+window launch uses window_decode_kernel: short caches with
@@ -581,6 +646,24 @@ int launch(Params& p, const Split& s, const void* k, const void* v, int64_t cap,
   return NSA_OK;
 }
 
+// Parameters shared by the sink+window entry points.
+int sparse_params(const void* q, const void* k, const void* v, const void* o, int64_t batch, int64_t n_heads,
+                  int64_t n_kv_heads, int64_t head_dim, int64_t window, int64_t sink, float sm_scale, Params& p) {
+  int rc = check_common(q, k, v, o, batch, n_heads, n_kv_heads, head_dim);
+  if (rc) return rc;
+  if (window < 0 || sink < 0 || window + sink < 1 || window + sink > (int64_t(1) << 30))
+    return fail(NSA_ERR_INVALID, "need window, sink >= 0 and 1 <= window + sink <= 2^30");
+  p = Params{};
+  p.q = static_cast<const __half*>(q);
+  p.o = static_cast<__half*>(const_cast<void*>(o));
+  p.n_kv_heads = static_cast<int>(n_kv_heads);
+  p.mode = kSparse;
+  p.window = static_cast<int>(window);
+  p.sink = static_cast<int>(sink);
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  return NSA_OK;
+}
+
 }  // namespace
 }  // namespace nsa
 
@@ -623,24 +706,73 @@ int nsa_sparse_decode(const void* q, const void* k_cache, const void* v_cache, v
                       int64_t seq_len, const int64_t* seq_lens, const int32_t* ring_heads, float sm_scale,
                       void* workspace, size_t workspace_bytes_, nsa_stream_t stream) {
   clear_error();
-  int rc = check_common(q, k_cache, v_cache, o, batch, n_heads, n_kv_heads, head_dim);
-  if (rc) return rc;
-  if (window < 0 || sink < 0 || window + sink < 1 || window + sink > (int64_t(1) << 30))
-    return fail(NSA_ERR_INVALID, "need window, sink >= 0 and 1 <= window + sink <= 2^30");
-  if (seq_len < 0) return fail(NSA_ERR_INVALID, "seq_len must be >= 0");
   Params p{};
-  p.q = static_cast<const __half*>(q);
-  p.o = static_cast<__half*>(o);
-  p.n_kv_heads = static_cast<int>(n_kv_heads);
-  p.mode = kSparse;
+  int rc = sparse_params(q, k_cache, v_cache, o, batch, n_heads, n_kv_heads, head_dim, window, sink, sm_scale, p);
+  if (rc) return rc;
+  if (seq_len < 0) return fail(NSA_ERR_INVALID, "seq_len must be >= 0");
   p.seq_len = seq_len;
   p.seq_lens = seq_lens;
   p.ring_heads = ring_heads;
-  p.window = static_cast<int>(window);
-  p.sink = static_cast<int>(sink);
-  p.scale_log2 = sm_scale * 1.4426950408889634f;
   const Split s = plan(batch * n_kv_heads, window + sink);
   return launch(p, s, k_cache, v_cache, window + sink, workspace, workspace_bytes_, stream);
+}
+
+int nsa_ring_append(void* k_cache, void* v_cache, int64_t* unit_lens, const void* new_k, const void* new_v,
+                    int64_t batch, int64_t n_kv_heads, int64_t head_dim, int64_t window, int64_t sink,
+                    nsa_stream_t stream) {
+  clear_error();
+  if (!k_cache || !v_cache || !unit_lens || !new_k || !new_v) return fail(NSA_ERR_INVALID, "null pointer");
+  if (head_dim != kHeadDim) return fail(NSA_ERR_UNSUPPORTED, "head_dim must be 128");
+  if (batch < 0 || n_kv_heads <= 0 || window < 0 || sink < 0 || window + sink < 1 ||
+      window + sink > (int64_t(1) << 30))
+    return fail(NSA_ERR_INVALID, "need batch >= 0, n_kv_heads > 0, window, sink >= 0, 1 <= window + sink <= 2^30");
+  const int64_t units = batch * n_kv_heads;
+  if (units == 0) return NSA_OK;
+  if (units > 0x7fffffff) return fail(NSA_ERR_UNSUPPORTED, "too many units");
+  cudaError_t e = launch_kernel(ring_append_kernel, dim3(static_cast<unsigned>(units)), dim3(kHeadDim), 0, stream,
+                                static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), unit_lens,
+                                static_cast<const __half*>(new_k), static_cast<const __half*>(new_v),
+                                static_cast<int>(sink), static_cast<int>(window));
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? NSA_OK : cuda_fail(e, "ring_append_kernel launch");
+}
+
+int nsa_ring_decode(const void* q, const void* k_cache, const void* v_cache, void* o, int64_t batch, int64_t n_heads,
+                    int64_t n_kv_heads, int64_t head_dim, int64_t window, int64_t sink, const int64_t* unit_lens,
+                    float sm_scale, void* workspace, size_t workspace_bytes_, nsa_stream_t stream) {
+  clear_error();
+  if (!unit_lens) return fail(NSA_ERR_INVALID, "unit_lens must not be NULL");
+  Params p{};
+  int rc = sparse_params(q, k_cache, v_cache, o, batch, n_heads, n_kv_heads, head_dim, window, sink, sm_scale, p);
+  if (rc) return rc;
+  p.unit_lens = const_cast<int64_t*>(unit_lens);  // read only without new_k
+  const Split s = plan(batch * n_kv_heads, window + sink);
+  return launch(p, s, k_cache, v_cache, window + sink, workspace, workspace_bytes_, stream);
+}
+
+int nsa_ring_decode_step(const void* q, void* k_cache, void* v_cache, void* o, int64_t batch, int64_t n_heads,
+                         int64_t n_kv_heads, int64_t head_dim, int64_t window, int64_t sink, int64_t* unit_lens,
+                         const void* new_k, const void* new_v, float sm_scale, void* workspace,
+                         size_t workspace_bytes_, nsa_stream_t stream) {
+  clear_error();
+  if (!unit_lens || !new_k || !new_v) return fail(NSA_ERR_INVALID, "null pointer");
+  if (!aligned16(new_k) || !aligned16(new_v)) return fail(NSA_ERR_ALIGN, "new_k and new_v must be 16-byte aligned");
+  Params p{};
+  int rc = sparse_params(q, k_cache, v_cache, o, batch, n_heads, n_kv_heads, head_dim, window, sink, sm_scale, p);
+  if (rc) return rc;
+  const Split s = plan(batch * n_kv_heads, window + sink);
+  if (use_window_kernel(s.n_units, window + sink)) {  // one launch: the decode CTA of each unit appends
+    p.unit_lens = unit_lens;
+    p.new_k = static_cast<const __half*>(new_k);
+    p.new_v = static_cast<const __half*>(new_v);
+    p.k_w = static_cast<__half*>(k_cache);
+    p.v_w = static_cast<__half*>(v_cache);
+    return launch_window(p, s.n_units, k_cache, v_cache, window + sink, stream);
+  }
+  rc = nsa_ring_append(k_cache, v_cache, unit_lens, new_k, new_v, batch, n_kv_heads, head_dim, window, sink, stream);
+  if (rc) return rc;
+  return nsa_ring_decode(q, k_cache, v_cache, o, batch, n_heads, n_kv_heads, head_dim, window, sink, unit_lens,
+                         sm_scale, workspace, workspace_bytes_, stream);
 }
 
 }  // extern "C"

@@ -111,3 +111,98 @@ def sparse_decode_attention(q, k_cache, v_cache, seq_len, window, sink=SINK_SIZE
                                          float(sm_scale), ws.data_ptr(), ws.numel(),
                                          _lib.stream_handle(q.device)))
     return o
+
+
+class RingCache:
+    """fp16 sink + sliding-window KV cache managed on the device (no reference
+    counterpart: the reference rebuilds a compacted cache on the host,
+    test_sparse_correctness.py:51-72).
+
+    k/v: [B, Hkv, sink + window, 128] fp16; unit_lens: int64 [B*Hkv], the
+    tokens appended per (batch row, kv head).  Position p < sink lives in slot
+    p, position p >= sink in slot sink + (p - sink) % window (dropped when
+    window is 0): the ring layout of ``sparse_decode_attention`` with head
+    (len - sink) % window, whose attended set this cache reproduces exactly.
+    ``decode_step`` appends one token per unit and attends in one launch when
+    every unit gets its own CTA (see nsa_ring_decode_step)."""
+
+    def __init__(self, batch, n_kv_heads, window, sink=SINK_SIZE, device=None):
+        self.batch, self.n_kv_heads, self.window, self.sink = int(batch), int(n_kv_heads), int(window), int(sink)
+        _require(self.batch >= 0 and self.n_kv_heads > 0 and self.window >= 0 and self.sink >= 0
+                 and self.window + self.sink >= 1, "need batch >= 0, n_kv_heads > 0, window, sink >= 0")
+        self.device = torch.device(device if device is not None else "cuda")
+        _require(self.device.type == "cuda", "RingCache lives on a CUDA device (no CPU fallback)")
+        shape = (self.batch, self.n_kv_heads, self.sink + self.window, D_HEAD)
+        self.k = torch.zeros(shape, dtype=torch.float16, device=self.device)
+        self.v = torch.zeros(shape, dtype=torch.float16, device=self.device)
+        self.unit_lens = torch.zeros(self.batch * self.n_kv_heads, dtype=torch.int64, device=self.device)
+        self._ws_bytes = _lib.load().nsa_sparse_workspace_bytes(self.batch, self.n_kv_heads, self.window, self.sink)
+
+    def _check_token(self, new_k, new_v):
+        for name, t in (("new_k", new_k), ("new_v", new_v)):
+            _check_fp16_cuda(name, t, 3)
+            _require(tuple(t.shape) == (self.batch, self.n_kv_heads, D_HEAD),
+                     f"{name} must be [B, Hkv, {D_HEAD}], got {tuple(t.shape)}")
+
+    def _check_q(self, q):
+        _check_fp16_cuda("q", q, 3)
+        _require(tuple(q.shape) == (self.batch, 8 * self.n_kv_heads, D_HEAD),
+                 f"q must be [B, 8*Hkv, {D_HEAD}], got {tuple(q.shape)}")
+
+    def append(self, new_k, new_v):
+        """Store one token per (batch row, kv head): new_k/new_v [B, Hkv, 128] fp16."""
+        self._check_token(new_k, new_v)
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.load().nsa_ring_append(
+                self.k.data_ptr(), self.v.data_ptr(), self.unit_lens.data_ptr(), new_k.data_ptr(), new_v.data_ptr(),
+                self.batch, self.n_kv_heads, D_HEAD, self.window, self.sink, _lib.stream_handle(self.device)))
+
+    def attend(self, q, sm_scale=None):
+        """Decode q [B, 8*Hkv, 128] fp16 against the cache -> o like q."""
+        self._check_q(q)
+        o = torch.empty_like(q)
+        with torch.cuda.device(self.device):
+            ws = _lib.workspace(self.device, self._ws_bytes)
+            _lib.check(_lib.load().nsa_ring_decode(
+                q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), o.data_ptr(), self.batch, 8 * self.n_kv_heads,
+                self.n_kv_heads, D_HEAD, self.window, self.sink, self.unit_lens.data_ptr(),
+                float(D_HEAD ** -0.5 if sm_scale is None else sm_scale), ws.data_ptr(), ws.numel(),
+                _lib.stream_handle(self.device)))
+        return o
+
+    def decode_step(self, q, new_k, new_v, sm_scale=None):
+        """Append new_k/new_v, then attend q (one launch when possible)."""
+        self._check_token(new_k, new_v)
+        self._check_q(q)
+        o = torch.empty_like(q)
+        with torch.cuda.device(self.device):
+            ws = _lib.workspace(self.device, self._ws_bytes)
+            _lib.check(_lib.load().nsa_ring_decode_step(
+                q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), o.data_ptr(), self.batch, 8 * self.n_kv_heads,
+                self.n_kv_heads, D_HEAD, self.window, self.sink, self.unit_lens.data_ptr(), new_k.data_ptr(),
+                new_v.data_ptr(), float(D_HEAD ** -0.5 if sm_scale is None else sm_scale), ws.data_ptr(),
+                ws.numel(), _lib.stream_handle(self.device)))
+        return o
+
+    def load_history(self, k_hist, v_hist, seq_len):
+        """Set the cache to its state after appending positions [0, seq_len) of
+        k_hist/v_hist [B, Hkv, >= seq_len, 128] fp16 (one gather, no per-token
+        launches)."""
+        _check_fp16_cuda("k_hist", k_hist, 4)
+        _check_fp16_cuda("v_hist", v_hist, 4)
+        L, S, W = int(seq_len), self.sink, self.window
+        _require(k_hist.shape[2] >= L, "history shorter than seq_len")
+        self.unit_lens.fill_(L)
+        ns = min(L, S)
+        self.k[:, :, :ns] = k_hist[:, :, :ns]
+        self.v[:, :, :ns] = v_hist[:, :, :ns]
+        if W > 0 and L > S:
+            pos = torch.arange(max(S, L - W), L, device=self.device)
+            slots = S + (pos - S) % W
+            self.k[:, :, slots] = k_hist[:, :, pos]
+            self.v[:, :, slots] = v_hist[:, :, pos]
+
+    def ring_head(self) -> int:
+        """Ring head of a cache whose units all hold the same length."""
+        L = int(self.unit_lens[0].item())
+        return (L - self.sink) % self.window if (self.window > 0 and L > self.sink) else 0
