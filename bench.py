@@ -330,9 +330,29 @@ def main():
             e1.record(stream)
             torch.cuda.synchronize()
             attn_ms = e0.elapsed_time(e1) / steps_timed
+        # informational (kivi): all layers' steps in one launch per rotation
+        # (decode_step_layers), for decode loops that have every layer's query at once
+        layered_ms = None
+        if name == "kivi" and wlobj.launches_per_step == 1:
+            kv = importlib.import_module("numerics-and-sparse-attn_b200.kivi")
+            g_lay = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_lay, stream=stream):
+                for _ in range(per_graph // n):
+                    kv.decode_step_layers(wlobj.layers, wlobj.q, wlobj.new_k, wlobj.new_v)
+            g_lay.replay()
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(n_graphs):
+                g_lay.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            layered_ms = e0.elapsed_time(e1) / steps_timed
+            del g_lay
         barrier()
         step_ms = max_over_ranks(step_ms)
         attn_ms = max_over_ranks(attn_ms)
+        if layered_ms is not None:
+            layered_ms = max_over_ranks(layered_ms)
 
         # e2e through the public API: pinned host q (and new token) in, o out
         q_h = [x.cpu().pin_memory() for x in wlobj.q]
@@ -404,6 +424,12 @@ def main():
         "e2e": {"value": B_PER_GPU * world / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "path": "public Python API per call"},
         "gpu_launches": steps_timed * wlobj.launches_per_step,
+        **({"layer_batched": {
+            "layers_per_launch": wlobj.n_layers, "us_per_layer_step": layered_ms * 1e3,
+            "tokens_per_s_per_layer": B_PER_GPU * world / (layered_ms * 1e-3),
+            "hbm_tbs": algorithmic_bytes(name, B_PER_GPU) / (layered_ms * 1e-3) / 1e12,
+            "note": "informational: every layer's decode step (same inputs as the headline) in one launch "
+                    "(decode_step_layers); needs all layers' queries at once"}} if layered_ms is not None else {}),
         "clocks": clocks.summary(),
         "verified": verified,
     }

@@ -228,6 +228,17 @@ int nsa_kivi_stream_decode(const nsa_kivi_stream_cache* cache, const void* q, vo
 int nsa_kivi_stream_decode_step(const nsa_kivi_stream_cache* cache, const void* new_k, const void* new_v,
                                 const void* q, void* o, float sm_scale, void* workspace, size_t workspace_bytes,
                                 nsa_stream_t stream);
+/* nsa_kivi_stream_decode_step for n_layers caches of one geometry (caches:
+ * host array of n_layers descriptors; new_k, new_v, q, o: host arrays of
+ * n_layers device pointers), results as n_layers separate calls.  When the
+ * step runs in one launch per layer, up to 24 layers share one launch
+ * (layer-major CTAs): the launch's fixed costs are paid once.  For decode
+ * loops that have every layer's query at once.  The workspace is the
+ * single-layer one.  No reference counterpart. */
+int nsa_kivi_stream_decode_step_layers(const nsa_kivi_stream_cache* caches, int64_t n_layers,
+                                       const void* const* new_k, const void* const* new_v, const void* const* q,
+                                       void* const* o, float sm_scale, void* workspace, size_t workspace_bytes,
+                                       nsa_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -8,8 +8,8 @@ The kernels live in ``libnsa_b200.so`` (C ABI: include/nsa_b200.h), built by
 from . import _lib
 from .constants import *  # noqa: F401,F403
 from .decode import RingCache, dense_decode_attention, sparse_decode_attention
-from .kivi import (KiviCache, build_quantized_kv_cache, dequantize_k, dequantize_v, quantize_k_cache,
-                   quantize_v_cache, sparse_decode_attention_quantized)
+from .kivi import (KiviCache, build_quantized_kv_cache, decode_step_layers, dequantize_k, dequantize_v,
+                   quantize_k_cache, quantize_v_cache, sparse_decode_attention_quantized)
 
 __all__ = [
     "dense_decode_attention",
@@ -21,6 +21,7 @@ __all__ = [
     "dequantize_k",
     "dequantize_v",
     "KiviCache",
+    "decode_step_layers",
     "RingCache",
     "native_library_path",
     "device_error",

@@ -53,6 +53,7 @@ PROTOTYPES = {
     "nsa_kivi_stream_workspace_bytes": (_SZ, [_P]),
     "nsa_kivi_stream_decode": (_INT, [_P, _P, _P, _F, _P, _SZ, _P]),
     "nsa_kivi_stream_decode_step": (_INT, [_P, _P, _P, _P, _P, _F, _P, _SZ, _P]),
+    "nsa_kivi_stream_decode_step_layers": (_INT, [_P, _I64, _P, _P, _P, _P, _F, _P, _SZ, _P]),
     "nsa_ring_append": (_INT, [_P, _P, _P, _P, _P] + [_I64] * 5 + [_P]),
     "nsa_ring_decode": (_INT, [_P, _P, _P, _P] + [_I64] * 6 + [_P, _F, _P, _SZ, _P]),
     "nsa_ring_decode_step": (_INT, [_P, _P, _P, _P] + [_I64] * 6 + [_P, _P, _P, _F, _P, _SZ, _P]),

@@ -724,9 +724,10 @@ struct Issuer {
   }
 };
 
-__global__ void __launch_bounds__(kThreads, kCtasPerSm)
-    kivi_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                       const KParams p) {
+// The work of CTA `bid` of one layer's launch (tensor maps and parameters in
+// kernel-parameter space).
+__device__ __forceinline__ void kivi_decode_cta(const CUtensorMap& tmK, const CUtensorMap& tmV, const KParams& p,
+                                                int64_t bid) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   grid_launch_dependents();
   grid_dependency_wait();  // the cache and q may come from the previous kernel of the stream
@@ -736,8 +737,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   }
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t unit = blockIdx.x / p.ppu;
-  const int piece = static_cast<int>(blockIdx.x % p.ppu);
+  const int64_t unit = bid / p.ppu;
+  const int piece = static_cast<int>(bid % p.ppu);
   // this piece's items [t_begin, t_end): item 0 = Q-batch 0, items 1..n_ft =
   // F-tiles 0..n_ft-1, item n_ft + b = Q-batch b (b >= 1)
   const int t_begin = piece * p.items / p.ppu, t_end = (piece + 1) * p.items / p.ppu;
@@ -962,6 +963,31 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   }
 }
 
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
+    kivi_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                       const KParams p) {
+  kivi_decode_cta(tmK, tmV, p, blockIdx.x);
+}
+
+// Several layers (caches of one geometry) in one launch: layer-major CTAs,
+// `per_layer` of them per layer.  Amortises the launch's fixed costs (start,
+// first-byte latency, tail) over all layers when the decode loop has every
+// layer's query at once.
+constexpr int kMaxLayers = 24;
+struct KiviLayers {
+  CUtensorMap tmK[kMaxLayers];
+  CUtensorMap tmV[kMaxLayers];
+  KParams p[kMaxLayers];
+  int64_t per_layer;
+  int n_layers;
+};
+static_assert(sizeof(KiviLayers) <= 32000, "kernel parameter space");
+
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) kivi_decode_layers_kernel(const __grid_constant__ KiviLayers L) {
+  const int layer = static_cast<int>(blockIdx.x / L.per_layer);
+  kivi_decode_cta(L.tmK[layer], L.tmV[layer], L.p[layer], blockIdx.x % L.per_layer);
+}
+
 struct Plan {
   int64_t n_units, grid;
   int n_qb, n_ft, items, ppu;
@@ -978,6 +1004,8 @@ int64_t cta_slots() {
   if (!slots[dev]) {
     int per_sm = 0;
     if (cudaFuncSetAttribute(kivi_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(kivi_decode_layers_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemBytes)) != cudaSuccess ||
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kivi_decode_kernel, kThreads, kSmemBytes) !=
             cudaSuccess ||
@@ -1013,9 +1041,10 @@ size_t ws_bytes(const Plan& s) {
   return counters + lse + pieces * kGroupHeads * kHeadDim * sizeof(float);
 }
 
-int launch(KParams& p, const Plan& s, const void* k_res, const void* v_res, void* ws, size_t wsb,
-           cudaStream_t stream) {
-  if (s.n_units == 0) return NSA_OK;
+// Completes p for plan s (workspace carving, device error word) and encodes
+// the residual tensor maps.
+int prepare(KParams& p, const Plan& s, const void* k_res, const void* v_res, void* ws, size_t wsb, CUtensorMap& mk,
+            CUtensorMap& mv) {
   const size_t need = ws_bytes(s);
   if (!ws || wsb < need)
     return fail(NSA_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, ws ? wsb : size_t(0));
@@ -1035,17 +1064,22 @@ int launch(KParams& p, const Plan& s, const void* k_res, const void* v_res, void
   p.ppu = s.ppu;
   p.err = device_error_word();
   if (!p.err) return fail(NSA_ERR_CUDA, "device error word unavailable");
-
   // residual [units][res_cap][128] viewed as [units][2 halves][res_cap][64] (dims
   // innermost first): one box brings 80 slots x both 64-dim halves, each half a
   // 128-byte-swizzled region of 80 rows
-  CUtensorMap mk, mv;
   const uint64_t dims[4] = {64, static_cast<uint64_t>(p.res_cap), 2, static_cast<uint64_t>(s.n_units)};
   const uint64_t strides[3] = {kHeadDim * 2, 128, static_cast<uint64_t>(p.res_cap) * kHeadDim * 2};
   const uint32_t box[4] = {64, kFRows, 2, 1};
   int rc = encode_tiled(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, k_res, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = encode_tiled(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, v_res, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  return encode_tiled(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, v_res, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int launch(KParams& p, const Plan& s, const void* k_res, const void* v_res, void* ws, size_t wsb,
+           cudaStream_t stream) {
+  if (s.n_units == 0) return NSA_OK;
+  CUtensorMap mk, mv;
+  int rc = prepare(p, s, k_res, v_res, ws, wsb, mk, mv);
   if (rc) return rc;
   cta_slots();  // sets the shared-memory limit
   cudaError_t e = launch_kernel(kivi_decode_kernel, dim3(static_cast<unsigned>(s.grid)), dim3(kThreads), kSmemBytes,
@@ -1233,6 +1267,62 @@ int nsa_kivi_stream_decode_step(const nsa_kivi_stream_cache* cache, const void* 
   rc = nsa_kivi_append(cache, new_k, new_v, stream);
   if (rc) return rc;
   return nsa_kivi_stream_decode(cache, q, o, sm_scale, workspace, workspace_bytes, stream);
+}
+
+int nsa_kivi_stream_decode_step_layers(const nsa_kivi_stream_cache* caches, int64_t n_layers,
+                                       const void* const* new_k, const void* const* new_v, const void* const* q,
+                                       void* const* o, float sm_scale, void* workspace, size_t workspace_bytes,
+                                       nsa_stream_t stream) {
+  clear_error();
+  if (n_layers < 0) return fail(NSA_ERR_INVALID, "n_layers must be >= 0");
+  if (n_layers == 0) return NSA_OK;
+  if (!caches || !new_k || !new_v || !q || !o) return fail(NSA_ERR_INVALID, "null pointer");
+  const nsa_kivi_stream_cache& c0 = caches[0];
+  for (int64_t l = 0; l < n_layers; ++l) {
+    const nsa_kivi_stream_cache& c = caches[l];
+    int rc = kivi_check_stream_cache(c);
+    if (rc) return rc;
+    if (c.batch != c0.batch || c.n_kv_heads != c0.n_kv_heads || c.window != c0.window || c.sink != c0.sink ||
+        c.residual != c0.residual)
+      return fail(NSA_ERR_INVALID, "all layers' caches must have the geometry of layer 0");
+    if (!all_aligned({q[l], o[l], new_k[l], new_v[l]}))
+      return fail(NSA_ERR_ALIGN, "q, o, new_k and new_v of every layer must be non-null and 16-byte aligned");
+  }
+  const Plan s = stream_plan(c0);
+  if (s.n_units == 0) return NSA_OK;
+  if (s.ppu != 1 || !fused_append_enabled() || s.grid * kMaxLayers > 0x7fffffff) {
+    for (int64_t l = 0; l < n_layers; ++l) {  // one step per layer
+      int rc = nsa_kivi_stream_decode_step(&caches[l], new_k[l], new_v[l], q[l], o[l], sm_scale, workspace,
+                                           workspace_bytes, stream);
+      if (rc) return rc;
+    }
+    return NSA_OK;
+  }
+  static thread_local KiviLayers L;  // ~19 KB: kept off the stack
+  cta_slots();
+  for (int64_t l0 = 0; l0 < n_layers; l0 += kMaxLayers) {
+    const int n = static_cast<int>(n_layers - l0 < kMaxLayers ? n_layers - l0 : kMaxLayers);
+    for (int i = 0; i < n; ++i) {
+      const nsa_kivi_stream_cache& c = caches[l0 + i];
+      KParams& p = L.p[i];
+      stream_params(c, q[l0 + i], o[l0 + i], sm_scale, p);
+      p.new_k = static_cast<const __half*>(new_k[l0 + i]);
+      p.new_v = static_cast<const __half*>(new_v[l0 + i]);
+      p.k_res = static_cast<__half*>(c.k_res);
+      p.v_res = static_cast<__half*>(c.v_res);
+      p.sink_k16 = static_cast<__half*>(c.sink_k);
+      p.sink_v16 = static_cast<__half*>(c.sink_v);
+      int rc = prepare(p, s, c.k_res, c.v_res, workspace, workspace_bytes, L.tmK[i], L.tmV[i]);
+      if (rc) return rc;
+    }
+    L.per_layer = s.grid;
+    L.n_layers = n;
+    cudaError_t e = launch_kernel(kivi_decode_layers_kernel, dim3(static_cast<unsigned>(s.grid * n)), dim3(kThreads),
+                                  kSmemBytes, stream, L);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "kivi_decode_layers_kernel launch");
+  }
+  return NSA_OK;
 }
 
 }  // extern "C"

@@ -198,6 +198,35 @@ class KiviStreamCacheDesc(ctypes.Structure):
                                                "v_win_packed", "v_win_scale", "v_win_zero", "k_res", "v_res")]
 
 
+def decode_step_layers(caches, qs, new_ks, new_vs, sm_scale=None):
+    """KiviCache.decode_step for several layers' caches (one geometry) at once:
+    returns the list of outputs.  Up to 24 layers share one kernel launch
+    (nsa_kivi_stream_decode_step_layers) when the step fits one launch per layer."""
+    n = len(caches)
+    _req(len(qs) == n and len(new_ks) == n and len(new_vs) == n, "one q, new_k and new_v per cache")
+    if n == 0:
+        return []
+    c0 = caches[0]
+    for c, q, nk, nv in zip(caches, qs, new_ks, new_vs):
+        _req(isinstance(c, KiviCache) and c.device == c0.device, "caches must be KiviCaches on one device")
+        for name, t, shape in (("q", q, (c.batch, 8 * c.n_kv_heads, c.head_dim)),
+                               ("new_k", nk, (c.batch, c.n_kv_heads, c.head_dim)),
+                               ("new_v", nv, (c.batch, c.n_kv_heads, c.head_dim))):
+            _req(isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == torch.float16 and t.is_contiguous()
+                 and tuple(t.shape) == shape, f"{name} must be a contiguous float16 CUDA tensor of shape {shape}")
+    if sm_scale is None:
+        sm_scale = c0.head_dim ** -0.5
+    outs = [torch.empty_like(q) for q in qs]
+    descs = (KiviStreamCacheDesc * n)(*[c._desc for c in caches])
+    ptrs = lambda ts: (ctypes.c_void_p * n)(*[t.data_ptr() for t in ts])  # noqa: E731
+    with torch.cuda.device(c0.device):
+        ws = _lib.workspace(c0.device, c0._ws_bytes)
+        _lib.check(_lib.load().nsa_kivi_stream_decode_step_layers(
+            descs, n, ptrs(new_ks), ptrs(new_vs), ptrs(qs), ptrs(outs), float(sm_scale), ws.data_ptr(), ws.numel(),
+            _lib.stream_handle(c0.device)))
+    return outs
+
+
 class KiviCache:
     """Streaming KIVI cache for one attention layer (see nsa_kivi_stream_cache).
 

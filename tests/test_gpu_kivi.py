@@ -291,6 +291,34 @@ def test_fused_step_equals_append_then_attend(W):
                 np.testing.assert_array_equal(a[key], b[key], err_msg=f"{key} at L={L}")
 
 
+def test_layer_batched_step_equals_per_layer_steps():
+    """decode_step_layers (3 layers in one launch) gives the same outputs and
+    cache states, bit for bit, as KiviCache.decode_step layer by layer, over
+    steps that include a group flush."""
+    import importlib
+    kivi = importlib.import_module("numerics-and-sparse-attn_b200.kivi")
+    B, Hkv, W, L, n = 32, 8, 256, 163_840, 3
+
+    def make():
+        g = torch.Generator(device=DEV).manual_seed(123)
+        return [kivi.KiviCache.synthetic(B, Hkv, W, L, device=DEV, generator=g) for _ in range(n)]
+
+    batched, single = make(), make()
+    g = torch.Generator(device=DEV).manual_seed(7)
+    for step in range(36):
+        qs = [torch.randn(B, 64, 128, device=DEV, generator=g).half() for _ in range(n)]
+        nks = [torch.randn(B, Hkv, 128, device=DEV, generator=g).half() for _ in range(n)]
+        nvs = [torch.randn(B, Hkv, 128, device=DEV, generator=g).half() for _ in range(n)]
+        outs = kivi.decode_step_layers(batched, qs, nks, nvs)
+        for layer in range(n):
+            ref = single[layer].decode_step(qs[layer], nks[layer], nvs[layer])
+            assert torch.equal(outs[layer], ref), (step, layer)
+    for a, b in zip(batched, single):
+        sa, sb = _state_np(a), _state_np(b)
+        for key in sa:
+            np.testing.assert_array_equal(sa[key], sb[key], err_msg=key)
+
+
 def test_no_device_error_recorded():
     import importlib
     pkg = importlib.import_module("numerics-and-sparse-attn_b200")
