@@ -354,13 +354,19 @@ def main():
         if layered_ms is not None:
             layered_ms = max_over_ranks(layered_ms)
 
-        # e2e through the public API: pinned host q (and new token) in, o out
-        q_h = [x.cpu().pin_memory() for x in wlobj.q]
-        o_h = torch.empty_like(q_h[0]).pin_memory()
-        if name == "kivi":
-            nk_h = [x.cpu().pin_memory() for x in wlobj.new_k]
-            nv_h = [x.cpu().pin_memory() for x in wlobj.new_v]
-        h2d = q_h[0].numel() * 2 + (2 * wlobj.new_k[0].numel() * 2 if name == "kivi" else 0)
+        # e2e through the public API: each step's inputs (q, and for kivi the new
+        # token's K and V) staged in one pinned host buffer and copied in with one
+        # H2D copy; the output copied back to pinned host memory
+        parts = [wlobj.q] + ([wlobj.new_k, wlobj.new_v] if name == "kivi" else [])
+        x_h = [torch.cat([p_[j].flatten() for p_ in parts]).cpu().pin_memory() for j in range(wlobj.n_layers)]
+        x_d = torch.empty_like(x_h[0], device=dev)
+        views, off = [], 0
+        for p_ in parts:
+            views.append(x_d[off:off + p_[0].numel()].view(p_[0].shape))
+            off += p_[0].numel()
+        o_d = torch.empty_like(wlobj.q[0])
+        o_h = torch.empty_like(o_d, device="cpu").pin_memory()
+        h2d = x_h[0].numel() * 2
         d2h = o_h.numel() * 2
         e2e_steps = min(a.steps, 200)
         barrier()
@@ -368,11 +374,12 @@ def main():
         e0.record(stream)
         for i in range(e2e_steps):
             j = i % wlobj.n_layers
-            qd = q_h[j].to(dev, non_blocking=True)
+            x_d.copy_(x_h[j], non_blocking=True)
             if name == "kivi":
-                o = wlobj.step(i, qd, nk_h[j].to(dev, non_blocking=True), nv_h[j].to(dev, non_blocking=True))
+                o = wlobj.layers[j].decode_step(views[0], views[1], views[2], out=o_d)
+                wlobj.out[j] = o
             else:
-                o = wlobj.step(i, qd)
+                o = wlobj.step(i, views[0])
             o_h.copy_(o, non_blocking=True)
         e1.record(stream)
         torch.cuda.synchronize()

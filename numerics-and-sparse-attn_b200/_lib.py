@@ -7,6 +7,7 @@ from the CUDA runtime RuntimeError.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 import threading
@@ -117,10 +118,17 @@ _ws_lock = threading.Lock()
 _workspaces: dict = {}
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+def on_device(device: torch.device):
+    """torch.cuda.device(device), or no context when it is already current."""
+    if device.index is None or torch.cuda.current_device() == device.index:
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
+
+
+def workspace(device: torch.device, nbytes: int, stream: int | None = None) -> torch.Tensor:
     """Zero-initialised scratch buffer for split-K partials and tickets, one
     per (device, stream); the kernels leave its counters zeroed again."""
-    key = (device.index, stream_handle(device))
+    key = (device.index, stream_handle(device) if stream is None else stream)
     with _ws_lock:
         ws = _workspaces.get(key)
         if ws is None or ws.numel() < nbytes:

@@ -60,11 +60,11 @@ def dense_decode_attention(q, k, v, seq_len, sm_scale=None):
     o = torch.empty_like(q)
     lib = _lib.load()
     ws_bytes = lib.nsa_dense_workspace_bytes(b, hkv, seq_len)
-    with torch.cuda.device(q.device):
-        ws = _lib.workspace(q.device, ws_bytes)
+    with _lib.on_device(q.device):
+        stream = _lib.stream_handle(q.device)
+        ws = _lib.workspace(q.device, ws_bytes, stream)
         _lib.check(lib.nsa_dense_decode(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), b, h, hkv, d,
-                                        k.shape[2], seq_len, float(sm_scale), ws.data_ptr(), ws.numel(),
-                                        _lib.stream_handle(q.device)))
+                                        k.shape[2], seq_len, float(sm_scale), ws.data_ptr(), ws.numel(), stream))
     return o
 
 
@@ -104,12 +104,12 @@ def sparse_decode_attention(q, k_cache, v_cache, seq_len, window, sink=SINK_SIZE
     o = torch.empty_like(q)
     lib = _lib.load()
     ws_bytes = lib.nsa_sparse_workspace_bytes(b, hkv, window, sink)
-    with torch.cuda.device(q.device):
-        ws = _lib.workspace(q.device, ws_bytes)
+    with _lib.on_device(q.device):
+        stream = _lib.stream_handle(q.device)
+        ws = _lib.workspace(q.device, ws_bytes, stream)
         _lib.check(lib.nsa_sparse_decode(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), o.data_ptr(), b, h,
                                          hkv, d, window, sink, seq_len, lens_ptr or None, heads_ptr or None,
-                                         float(sm_scale), ws.data_ptr(), ws.numel(),
-                                         _lib.stream_handle(q.device)))
+                                         float(sm_scale), ws.data_ptr(), ws.numel(), stream))
     return o
 
 

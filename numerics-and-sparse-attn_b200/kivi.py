@@ -327,9 +327,10 @@ class KiviCache:
         units = self.batch * self.n_kv_heads
         return 1 if units >= slots or 2 * units > slots else 2
 
-    def decode_step(self, q, new_k, new_v, sm_scale=None):
+    def decode_step(self, q, new_k, new_v, sm_scale=None, out=None):
         """One decode step: quantize-on-append of the new token, then attend
-        (one launch when every unit gets its own CTA, else append + attend)."""
+        (one launch when every unit gets its own CTA, else append + attend).
+        ``out`` (optional): preallocated output like q."""
         shape = (self.batch, self.n_kv_heads, self.head_dim)
         for name, t in (("new_k", new_k), ("new_v", new_v)):
             _req(isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == torch.float16 and t.is_contiguous()
@@ -337,15 +338,20 @@ class KiviCache:
         _req(isinstance(q, torch.Tensor) and q.is_cuda and q.dtype == torch.float16 and q.is_contiguous()
              and tuple(q.shape) == (self.batch, 8 * self.n_kv_heads, self.head_dim),
              "q must be a contiguous float16 CUDA tensor [B, 8*Hkv, 128]")
+        if out is None:
+            out = torch.empty_like(q)
+        else:
+            _req(isinstance(out, torch.Tensor) and out.is_cuda and out.dtype == torch.float16
+                 and out.is_contiguous() and out.shape == q.shape, "out must be a contiguous float16 CUDA tensor like q")
         if sm_scale is None:
             sm_scale = self.head_dim ** -0.5
-        o = torch.empty_like(q)
-        with torch.cuda.device(self.device):
-            ws = _lib.workspace(self.device, self._ws_bytes)
+        with _lib.on_device(self.device):
+            stream = _lib.stream_handle(self.device)
+            ws = _lib.workspace(self.device, self._ws_bytes, stream)
             _lib.check(_lib.load().nsa_kivi_stream_decode_step(
-                ctypes.byref(self._desc), new_k.data_ptr(), new_v.data_ptr(), q.data_ptr(), o.data_ptr(),
-                float(sm_scale), ws.data_ptr(), ws.numel(), _lib.stream_handle(self.device)))
-        return o
+                ctypes.byref(self._desc), new_k.data_ptr(), new_v.data_ptr(), q.data_ptr(), out.data_ptr(),
+                float(sm_scale), ws.data_ptr(), ws.numel(), stream))
+        return out
 
     # ---------------------------------------------------------------- filling
     def load_state(self, seq_len, sink_k, sink_v, tail_k=None, tail_v=None, tail_start=None):
