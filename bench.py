@@ -424,7 +424,10 @@ def main():
                      "traffic": None,
                      "kernel": ("kivi_decode_kernel (quantize-on-append + attention, one launch)"
                                 if wlobj.launches_per_step == 1 else "kivi_decode_kernel (attention)")
-                     if name == "kivi" else "fp16_decode_kernel",
+                     if name == "kivi" else
+                     ("window_decode_kernel (one CTA per unit)" if name == "sparse" and
+                      B_PER_GPU * HKV >= torch.cuda.get_device_properties(dev).multi_processor_count and
+                      S + WORKLOADS[name]["window"] <= 384 else "fp16_decode_kernel (persistent)"),
                      "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
                      else "fallback 6.65 TB/s", "kernel_us": attn_ms * 1e3,
                      "algorithmic_bytes_per_launch": bytes_step},
