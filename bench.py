@@ -63,6 +63,15 @@ def algorithmic_bytes(workload: str, batch: int) -> int:
     return int((18_612_224 + 24_576 * (w["window"] - R)) * scale)
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of ONE launch of the
+# dominant kernel at B=32, from the committed ncu captures of this exact workload.
+NCU_TRAFFIC = {
+    "kivi": (25_653_248, "profiles/kivi_decode_kernel_kivi_W256_L163840_B32.md"),
+    "sparse": (34_635_008, "profiles/window_decode_kernel_sparse_W256_L163840_B32.md"),
+    "dense": (1_078_491_176, "profiles/fp16_decode_kernel_dense_L8192_B32.md"),
+}
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -421,7 +430,9 @@ def main():
                        % (wlobj.n_layers, wlobj.n_layers * bytes_step / 1e6)),
         "hbm_tbs_step": bytes_step / (step_ms * 1e-3) / 1e12,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None,
+                     "traffic": (NCU_TRAFFIC[name][0] * B_PER_GPU // 32) if name in NCU_TRAFFIC else None,
+                     "traffic_source": (NCU_TRAFFIC[name][1] + " (one ncu capture, cold L2)")
+                     if name in NCU_TRAFFIC else None,
                      "kernel": ("kivi_decode_kernel (quantize-on-append + attention, one launch)"
                                 if wlobj.launches_per_step == 1 else "kivi_decode_kernel (attention)")
                      if name == "kivi" else
