@@ -195,7 +195,18 @@ int nsa_kivi_decode(const void* q, const void* k_res, const void* v_res,
  * min(len, sink) tokens and stream tokens with p >= len - W.  When
  * (len - sink - R) % 32 == 0 and len >= sink + W the state equals
  * build_quantized_kv_cache of the same window.  All pointers are device
- * memory; unit_lens holds the token count of every (batch, kv_head) unit. */
+ * memory; unit_lens holds the token count of every (batch, kv_head) unit.
+ *
+ * Memory format (chosen so that a batch of groups, or a run of residual
+ * slots, is one contiguous copy into shared memory):
+ *   groups: u8 [B, Hkv, 1 + NG, 3072], one record per quantized group,
+ *     record 0 the sink group, record 1 + s window slot s; a record holds
+ *     K codes u8 [8][D] at byte 0, K scale f16 [D] at 1024, K zero f16 [D]
+ *     at 1280, V codes u8 [32][D/4] at 1536, V scale f16 [32][D/32] at 2560,
+ *     V zero f16 [32][D/32] at 2816 -- the group's share of the reference's
+ *     k_/v_{sink,win}_{packed,scale,zero} tensors.
+ *   k_res, v_res: f16 [B, Hkv, R + 32, D]; slot r stores logical 16-byte
+ *     chunk c (channels 8c .. 8c+7) at chunk (c & 8) | ((c & 7) ^ (r & 7)). */
 typedef struct {
   int64_t batch, n_kv_heads, head_dim;  /* head_dim must be 128 */
   int64_t window, sink, residual;       /* W; S in [1, 32]; R a positive multiple of 32 */
@@ -203,11 +214,8 @@ typedef struct {
   int64_t* unit_lens;                   /* [B * Hkv] tokens appended so far */
   void* sink_k;                         /* f16 [B, Hkv, S, D] unquantized sink tokens */
   void* sink_v;
-  void* k_sink_packed, *k_sink_scale, *k_sink_zero;  /* u8 [B,Hkv,8,D]; f16 [B,Hkv,1,D] */
-  void* v_sink_packed, *v_sink_scale, *v_sink_zero;  /* u8 [B,Hkv,32,D/4]; f16 [B,Hkv,32,D/32] */
-  void* k_win_packed, *k_win_scale, *k_win_zero;     /* u8 [B,Hkv,NG*8,D]; f16 [B,Hkv,NG,D] */
-  void* v_win_packed, *v_win_scale, *v_win_zero;     /* u8 [B,Hkv,NG*32,D/4]; f16 [B,Hkv,NG*32,D/32] */
-  void* k_res, *v_res;                               /* f16 [B, Hkv, R + 32, D] */
+  void* groups;                         /* u8 [B, Hkv, 1 + NG, 3072] group records */
+  void* k_res, *v_res;                  /* f16 [B, Hkv, R + 32, D], chunk-permuted slots */
 } nsa_kivi_stream_cache;
 
 /* Append one token per (batch, kv_head): new_k, new_v f16 [B, Hkv, D];

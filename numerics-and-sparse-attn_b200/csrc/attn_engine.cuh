@@ -116,8 +116,9 @@ struct WarpAttn {
   }
 
   // Consume tokens [row0, row0+16) of a swizzled tile whose regions are
-  // `region_bytes` apart.  valid_lo / valid_hi: validity of rows row0+g and
-  // row0+g+8 for this lane (g = lane / 4).
+  // `region_bytes` apart (rows kRowBytes apart, see tile_off).  valid_lo /
+  // valid_hi: validity of rows row0+g and row0+g+8 for this lane (g = lane / 4).
+  template <uint32_t kRowBytes = 128>
   __device__ __forceinline__ void consume16(uint32_t kbase, uint32_t vbase, uint32_t region_bytes, int row0,
                                             bool valid_lo, bool valid_hi, float scale_log2, int lane) {
     float s[4] = {0.f, 0.f, 0.f, 0.f};
@@ -129,7 +130,7 @@ struct WarpAttn {
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         uint32_t a0, a1, a2, a3;
-        const uint32_t addr = kbase + (ks >> 2) * region_bytes + swz128(row, 2 * (ks & 3) + hi);
+        const uint32_t addr = kbase + tile_off<kRowBytes>(row, 8 * (ks >> 2) + 2 * (ks & 3) + hi, region_bytes);
         ldmatrix_x4(addr, a0, a1, a2, a3);
         if (ks & 1)
           mma_16816(s2, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
@@ -148,7 +149,7 @@ struct WarpAttn {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         uint32_t a0, a1, a2, a3;
-        const uint32_t addr = vbase + (j >> 2) * region_bytes + swz128(row, 2 * (j & 3) + hi);
+        const uint32_t addr = vbase + tile_off<kRowBytes>(row, 8 * (j >> 2) + 2 * (j & 3) + hi, region_bytes);
         ldmatrix_x4_trans(addr, a0, a1, a2, a3);
         mma_16816(acc[j], a0, a1, a2, a3, pb0, pb1);
       }
@@ -156,9 +157,10 @@ struct WarpAttn {
   }
 
   // Consume N blocks of 16 tokens, rows [row0, row0 + 16N) of a swizzled tile
-  // (regions `region_bytes` apart), with one softmax step for all of them.
-  // valid_lo[h] / valid_hi[h]: validity of rows row0+16h+g and row0+16h+g+8.
-  template <int N>
+  // (regions `region_bytes` apart, rows kRowBytes apart), with one softmax
+  // step for all of them.  valid_lo[h] / valid_hi[h]: validity of rows
+  // row0+16h+g and row0+16h+g+8.
+  template <int N, uint32_t kRowBytes = 128>
   __device__ __forceinline__ void consume_rows(uint32_t kbase, uint32_t vbase, uint32_t region_bytes, int row0,
                                                const bool (&valid_lo)[N], const bool (&valid_hi)[N], float scale_log2,
                                                int lane) {
@@ -175,7 +177,8 @@ struct WarpAttn {
         for (int h = 0; h < N; ++h) {
           const uint32_t row = row0 + 16 * h + ((lane >> 3) & 1) * 8 + (lane & 7);
           uint32_t a0, a1, a2, a3;
-          ldmatrix_x4(kbase + (ks >> 2) * region_bytes + swz128(row, 2 * (ks & 3) + hi), a0, a1, a2, a3);
+          ldmatrix_x4(kbase + tile_off<kRowBytes>(row, 8 * (ks >> 2) + 2 * (ks & 3) + hi, region_bytes), a0, a1, a2,
+                      a3);
           mma_16816((ks & 1) ? s2[h] : s[h], a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
         }
       }
@@ -193,7 +196,8 @@ struct WarpAttn {
       for (int h = 0; h < N; ++h) {
         const uint32_t row = row0 + 16 * h + (mi >> 1) * 8 + (lane & 7);
         uint32_t a0, a1, a2, a3;
-        ldmatrix_x4_trans(vbase + (j >> 2) * region_bytes + swz128(row, 2 * (j & 3) + (mi & 1)), a0, a1, a2, a3);
+        ldmatrix_x4_trans(vbase + tile_off<kRowBytes>(row, 8 * (j >> 2) + 2 * (j & 3) + (mi & 1), region_bytes), a0,
+                          a1, a2, a3);
         mma_16816(acc[j], a0, a1, a2, a3, pb[h][0], pb[h][1]);
       }
     }

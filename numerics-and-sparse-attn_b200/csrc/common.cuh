@@ -180,6 +180,16 @@ __device__ __forceinline__ uint32_t swz128(uint32_t row, uint32_t chunk) {
   return row * 128u + ((chunk ^ (row & 7u)) << 4);
 }
 
+// Byte offset of (row, 16-byte chunk c in 0..15) of a tile of 128-dim fp16
+// rows kept as two 128-byte halves, each swizzled as above.  kRowBytes = 128:
+// the halves are separate regions `region` bytes apart (the boxes of a TMA
+// SWIZZLE_128B load); kRowBytes = 256: they sit side by side in each row
+// (region = 128), as a contiguous copy of chunk-permuted rows leaves them.
+template <uint32_t kRowBytes>
+__device__ __forceinline__ uint32_t tile_off(uint32_t row, uint32_t chunk, uint32_t region) {
+  return (chunk >> 3) * region + row * kRowBytes + (((chunk & 7u) ^ (row & 7u)) << 4);
+}
+
 // Named barrier among the consumer warps only (the producer warp never joins).
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");

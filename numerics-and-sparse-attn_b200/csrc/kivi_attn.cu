@@ -10,12 +10,17 @@
 // other Q-batches, where
 //   Q-batch    up to 5 quantized 32-token groups (slot 0 of batch 0 is the
 //              padded sink group, then window groups in physical order), staged
-//              raw -- codes, scales, zero points -- by 1-D bulk copies, 3 KiB
-//              per group (Q ring, 2 x 15 KiB);
-//   F-tile     80 slots of the fp16 residual ring, K and V each staged by one
-//              TMA box (both 64-dim halves, 128-byte swizzle) (F ring, 2 x 40 KiB).
+//              raw -- codes, scales, zero points -- 3 KiB per group (Q ring,
+//              2 x 15 KiB);
+//   F-tile     80 slots of the fp16 residual ring, K and V (F ring, 2 x 40 KiB).
+// Staging depends on the layout (Lay): the streaming cache keeps each group's
+// six tensors in one record and its residual slots chunk-permuted
+// (kivi_format.cuh), so a Q-batch is ONE 1-D bulk copy and an F-tile one copy
+// each of K and V, landing bank-conflict free; the reference's separate
+// tensors take six bulk copies per Q-batch (one per tensor) and a TMA box per
+// F-tile (both 64-dim halves, 128-byte swizzle).
 // Batch 0 carries most of the arithmetic, so it is loaded and consumed first
-// and its dequantization overlaps the residual's transfer.  Every TMA request
+// and its dequantization overlaps the residual's transfer.  Every copy request
 // costs a fixed issue time (about 40 ns on B200) whatever its size, so loads
 // are few and large, and those that do not depend on the unit's length (query,
 // batch 0, residual) are issued before that length is read.  Q-batches after
@@ -39,12 +44,13 @@
 //      integer zero points, and the per-token scale is folded into the P
 //      fragment of each channel group (one rounding, as in an fp16
 //      dequantization of the cache).
-// F-tiles go through the shared fp16 engine (consume16).
+// F-tiles go through the shared fp16 engine (consume_rows).
 #include <cstddef>
 #include <cstdlib>
 
 #include "attn_engine.cuh"
 #include "host_util.h"
+#include "kivi_format.cuh"
 #include "quant_math.cuh"
 
 namespace nsa {
@@ -60,13 +66,35 @@ constexpr uint32_t kFStageBytes = 2 * kFTile;  // 40 KiB
 constexpr int kFStages = 2;
 constexpr int kQStages = 2;
 constexpr int kBatchGroups = 5;            // quantized groups per Q-batch
-constexpr uint32_t kQBytes = kGroupHeads * kHeadDim * 2;
 constexpr int kQPadStride = kHeadDim + 8;  // 272-byte rows: 8 rows of an ldmatrix hit distinct banks
 // Q-batch stage layout (byte offsets); one slot per group
 constexpr uint32_t kOffKP = 0, kOffKS = kBatchGroups * 1024, kOffKZ = kOffKS + kBatchGroups * 256,
                    kOffVP = kOffKZ + kBatchGroups * 256, kOffVS = kOffVP + kBatchGroups * 1024,
                    kOffVZ = kOffVS + kBatchGroups * 256;
 constexpr uint32_t kQStageBytes = kOffVZ + kBatchGroups * 256;  // 3 KiB per group
+static_assert(kQStageBytes == kBatchGroups * kRecBytes, "a Q stage holds 5 group records");
+
+// Staging of one cache layout.  kRec: the streaming cache (group records, a
+// batch one bulk copy, record-major Q stage; chunk-permuted residual rows, an
+// F-tile one bulk copy each of K and V, 256-byte rows in shared memory).
+// Otherwise the reference's separate tensors (field-major Q stage, six bulk
+// copies per batch; F-tiles by TMA boxes, two 128-byte-swizzled regions).
+template <bool kRec>
+struct Lay {
+  static constexpr uint32_t kRowBytes = kRec ? 256 : 128;
+  static constexpr uint32_t kRegion = kRec ? 128 : kFRegion;
+  // Q stage: byte offsets of batch slot gs's fields
+  static __device__ __forceinline__ uint32_t kp(int gs) { return kRec ? gs * kRecBytes + kRecKP : gs * 1024; }
+  static __device__ __forceinline__ uint32_t ks(int gs) { return kRec ? gs * kRecBytes + kRecKS : kOffKS + gs * 256; }
+  static __device__ __forceinline__ uint32_t kz(int gs) { return kRec ? gs * kRecBytes + kRecKZ : kOffKZ + gs * 256; }
+  static __device__ __forceinline__ uint32_t vp(int gs) { return kRec ? gs * kRecBytes + kRecVP : kOffVP + gs * 1024; }
+  static __device__ __forceinline__ uint32_t vs(int gs) { return kRec ? gs * kRecBytes + kRecVS : kOffVS + gs * 256; }
+  static __device__ __forceinline__ uint32_t vz(int gs) { return kRec ? gs * kRecBytes + kRecVZ : kOffVZ + gs * 256; }
+  // F-tile (K at 0, V at kFTile): (row, 16-byte chunk 0..15)
+  static __device__ __forceinline__ uint32_t f(uint32_t row, uint32_t chunk) {
+    return tile_off<kRowBytes>(row, chunk, kRegion);
+  }
+};
 
 struct KiviMeta {
   int32_t n_sink;    // attended sink tokens
@@ -124,6 +152,7 @@ struct KParams {
   const uint8_t* vw_p;
   const __half* vw_s;
   const __half* vw_z;
+  uint8_t* grp;  // stream layout: group records (kivi_format.cuh)
   int* counters;
   float* part_lse;
   float* part_o;
@@ -300,6 +329,7 @@ __device__ __forceinline__ uint32_t chunk_off(int i) { return (i >> 1) * 128 + (
 // Attend to the attended tokens (`mask`) of the quantized group in batch slot
 // `gs` of the Q stage at `qs`.  qrow: this lane's query row Q[head g] + 32t
 // bytes in shared memory (chunks at chunk_off).
+template <bool kRec>
 __device__ __forceinline__ void attend_group(WarpAttn& st, uint32_t qrow, const LaneQ& lq, uint32_t qs, int gs,
                                              uint32_t mask, float scale_log2, int lane) {
   const int g = lane >> 2, t = lane & 3;
@@ -311,13 +341,13 @@ __device__ __forceinline__ void attend_group(WarpAttn& st, uint32_t qrow, const 
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       uint32_t s0, s1, s2, s3, q0, q1, q2, q3;
-      lds128(qs + kOffKS + gs * 256 + 32 * t + chunk_off(i), s0, s1, s2, s3);
+      lds128(qs + Lay<kRec>::ks(gs) + 32 * t + chunk_off(i), s0, s1, s2, s3);
       lds128(qrow + chunk_off(i), q0, q1, q2, q3);
       sq[4 * i] = hmul2u(q0, s0);
       sq[4 * i + 1] = hmul2u(q1, s1);
       sq[4 * i + 2] = hmul2u(q2, s2);
       sq[4 * i + 3] = hmul2u(q3, s3);
-      lds128(qs + kOffKZ + gs * 256 + 32 * t + chunk_off(i), zn[4 * i], zn[4 * i + 1], zn[4 * i + 2],
+      lds128(qs + Lay<kRec>::kz(gs) + 32 * t + chunk_off(i), zn[4 * i], zn[4 * i + 1], zn[4 * i + 2],
              zn[4 * i + 3]);
     }
     float zc[4] = {0.f, 0.f, 0.f, 0.f}, zc2[4] = {0.f, 0.f, 0.f, 0.f};  // two chains: half the mma latency
@@ -345,7 +375,7 @@ __device__ __forceinline__ void attend_group(WarpAttn& st, uint32_t qrow, const 
       s[hf][0] = s[hf][2] = -zb0;
       s[hf][1] = s[hf][3] = -zb1;
       s2[hf][0] = s2[hf][1] = s2[hf][2] = s2[hf][3] = 0.f;
-      const uint32_t src = qs + kOffKP + gs * 1024 + (4 * hf + (g >> 1)) * 128 + 16 * t;
+      const uint32_t src = qs + Lay<kRec>::kp(gs) + (4 * hf + (g >> 1)) * 128 + 16 * t;
       lds128(src, kw[hf][0], kw[hf][1], kw[hf][2], kw[hf][3]);
       lds128(src + 64, kw[hf][4], kw[hf][5], kw[hf][6], kw[hf][7]);
     }
@@ -377,13 +407,13 @@ __device__ __forceinline__ void attend_group(WarpAttn& st, uint32_t qrow, const 
 #pragma unroll
   for (int hf = 0; hf < 2; ++hf) {
     if (!hm[hf]) continue;
-    const uint32_t vrow = qs + kOffVP + gs * 1024 + 16 * hf * 32;
+    const uint32_t vrow = qs + Lay<kRec>::vp(gs) + 16 * hf * 32;
     uint32_t vs[4][2], vz[4][2];  // scales / zero points of tokens tv[k], channel groups (0,1), (2,3)
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int tok = 16 * hf + lq.tv[k];
-      lds64(qs + kOffVS + gs * 256 + tok * 8, vs[k][0], vs[k][1]);
-      lds64(qs + kOffVZ + gs * 256 + tok * 8, vz[k][0], vz[k][1]);
+      lds64(qs + Lay<kRec>::vs(gs) + tok * 8, vs[k][0], vs[k][1]);
+      lds64(qs + Lay<kRec>::vz(gs) + tok * 8, vz[k][0], vz[k][1]);
     }
     // unattended tokens: scale and zero 0, so that their terms are exactly 0
     // whatever the stored values (P is 0 there; this keeps inf / NaN out of P.V)
@@ -430,8 +460,8 @@ __device__ __forceinline__ void attend_group(WarpAttn& st, uint32_t qrow, const 
 
 // Zero the V rows of slots that are not attended, so stale or
 // uninitialised cache memory (possibly NaN) cannot reach the P.V product.
-__device__ __forceinline__ void zero_invalid_v_rows(uint32_t vbase, uint32_t region_bytes, int row0, bool v_lo,
-                                                    bool v_hi, int lane) {
+template <bool kRec>
+__device__ __forceinline__ void zero_invalid_v_rows(uint32_t vbase, int row0, bool v_lo, bool v_hi, int lane) {
   const unsigned bad = __ballot_sync(0xffffffffu, !(v_lo && v_hi));
   if (bad == 0) return;
   const int g = lane >> 2, t = lane & 3;
@@ -443,11 +473,10 @@ __device__ __forceinline__ void zero_invalid_v_rows(uint32_t vbase, uint32_t reg
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const uint32_t chunk = 4 * t + c;  // 0..15
-      const uint32_t a = vbase + (chunk >> 3) * region_bytes + swz128(row, chunk & 7);
-      asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(a), "r"(0u));
+      asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(vbase + Lay<kRec>::f(row, chunk)), "r"(0u));
     }
   }
-  fence_proxy_async_smem();  // the stage is refilled by TMA later
+  fence_proxy_async_smem();  // the stage is refilled by the async proxy later
   __syncwarp();
 }
 
@@ -510,17 +539,17 @@ __device__ __forceinline__ void patch_residual_row(uint32_t sd, int row, uint32_
   const int kv = lane >> 4, chunk = lane & 15;  // chunk: 8 channels
   uint32_t x, y, z, w;
   lds128(tok + kv * kHeadDim * 2 + chunk * 16, x, y, z, w);
-  sts128(sd + kv * kFTile + (chunk >> 3) * kFRegion + swz128(row, chunk & 7), x, y, z, w);
+  sts128(sd + kv * kFTile + Lay<true>::f(row, chunk), x, y, z, w);
   fence_proxy_async_smem();
   __syncwarp();
 }
 
 // One group record (K of channel c, V of token c/4 x channel group c%4) from
 // the group's 32 K values of channel c and 32 V values of its token and
-// channel group: into Q-stage slot `sl` at `qs` and to the cache arrays.
+// channel group: into Q-stage slot `sl` at `qs` and to the cache record `rec`.
 __device__ __forceinline__ void store_group_record(const float (&x)[32], const float (&y)[32], uint32_t qs, int sl,
-                                                   uint8_t* kp, __half* ks, __half* kz, uint8_t* vp, __half* vs,
-                                                   __half* vz, int c) {
+                                                   const GroupRec& rec, int c) {
+  using L = Lay<true>;
   float mn = INFINITY, mx = -INFINITY;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
@@ -529,17 +558,17 @@ __device__ __forceinline__ void store_group_record(const float (&x)[32], const f
   }
   GroupParams gp = group_params(mn, mx);
   const __half hs = __float2half_rn(gp.scale), hz = __float2half_rn(gp.zero);
-  ks[c] = hs;
-  kz[c] = hz;
-  sts16(qs + kOffKS + sl * 256 + c * 2, hs);
-  sts16(qs + kOffKZ + sl * 256 + c * 2, hz);
+  rec.ks[c] = hs;
+  rec.kz[c] = hz;
+  sts16(qs + L::ks(sl) + c * 2, hs);
+  sts16(qs + L::kz(sl) + c * 2, hz);
 #pragma unroll
   for (int bq = 0; bq < 8; ++bq) {
     uint32_t byte = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) byte |= code_of(x[4 * bq + j], gp) << (2 * j);
-    kp[bq * kHeadDim + c] = static_cast<uint8_t>(byte);
-    sts8(qs + kOffKP + sl * 1024 + bq * kHeadDim + c, byte);
+    rec.kp[bq * kHeadDim + c] = static_cast<uint8_t>(byte);
+    sts8(qs + L::kp(sl) + bq * kHeadDim + c, byte);
   }
   const int tok = c >> 2, q = c & 3;
   mn = INFINITY;
@@ -551,22 +580,22 @@ __device__ __forceinline__ void store_group_record(const float (&x)[32], const f
   }
   gp = group_params(mn, mx);
   const __half vhs = __float2half_rn(gp.scale), vhz = __float2half_rn(gp.zero);
-  vs[tok * 4 + q] = vhs;
-  vz[tok * 4 + q] = vhz;
-  sts16(qs + kOffVS + sl * 256 + (tok * 4 + q) * 2, vhs);
-  sts16(qs + kOffVZ + sl * 256 + (tok * 4 + q) * 2, vhz);
+  rec.vs[tok * 4 + q] = vhs;
+  rec.vz[tok * 4 + q] = vhz;
+  sts16(qs + L::vs(sl) + (tok * 4 + q) * 2, vhs);
+  sts16(qs + L::vz(sl) + (tok * 4 + q) * 2, vhz);
   uint32_t lo = 0, hi = 0;
 #pragma unroll
   for (int j = 0; j < 16; ++j) lo |= code_of(y[j], gp) << (2 * j);
 #pragma unroll
   for (int j = 0; j < 16; ++j) hi |= code_of(y[16 + j], gp) << (2 * j);
-  *reinterpret_cast<uint2*>(vp + tok * 32 + q * 8) = make_uint2(lo, hi);
-  sts64(qs + kOffVP + sl * 1024 + tok * 32 + q * 8, lo, hi);
+  *reinterpret_cast<uint2*>(rec.vp + tok * 32 + q * 8) = make_uint2(lo, hi);
+  sts64(qs + L::vp(sl) + tok * 32 + q * 8, lo, hi);
   fence_proxy_async_smem();
 }
 
 // The padded sink group of a unit holding n sink tokens (the n real ones,
-// then copies of token 0), into batch 0's slot 0 and the sink arrays.
+// then copies of token 0), into batch 0's slot 0 and the unit's record 0.
 __device__ __forceinline__ void requantize_sink(const KParams& p, int64_t unit, int n, uint32_t qs, int c) {
   const int S = p.sink;
   float x[32], y[32];
@@ -576,9 +605,7 @@ __device__ __forceinline__ void requantize_sink(const KParams& p, int64_t unit, 
   const __half* vrow = p.sink_v16 + (unit * S + (tok < n ? tok : 0)) * kHeadDim + q * 32;
 #pragma unroll
   for (int j = 0; j < 32; ++j) y[j] = __half2float(vrow[j]);
-  store_group_record(x, y, qs, 0, const_cast<uint8_t*>(p.ks_p) + unit * 1024, const_cast<__half*>(p.ks_s) + unit * 128,
-                     const_cast<__half*>(p.ks_z) + unit * 128, const_cast<uint8_t*>(p.vs_p) + unit * 1024,
-                     const_cast<__half*>(p.vs_s) + unit * 128, const_cast<__half*>(p.vs_z) + unit * 128, c);
+  store_group_record(x, y, qs, 0, group_rec(p.grp, unit, p.n_groups, 0), c);
 }
 
 // Stream group [base, base + 32) leaving the residual ring (slots s0 .. s0+31,
@@ -596,17 +623,17 @@ __device__ __forceinline__ void quantize_flushed_group(const KParams& p, int64_t
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const int slot = s0 + j, f = slot / kFRows, r = slot % kFRows;
-      const uint32_t a = f_stage0 + f * kFStageBytes + (c >> 6) * kFRegion + swz128(r, (c & 63) >> 3) + (c & 7) * 2;
+      const uint32_t a = f_stage0 + f * kFStageBytes + Lay<true>::f(r, c >> 3) + (c & 7) * 2;
       unsigned short h;
       asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(a));
       x[j] = __half2float(__ushort_as_half(h));
     }
     const int slot = s0 + tok, f = slot / kFRows, r = slot % kFRows;
-    const uint32_t vb = f_stage0 + f * kFStageBytes + kFTile + (q >> 1) * kFRegion;
+    const uint32_t vb = f_stage0 + f * kFStageBytes + kFTile;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {  // channels q*32 + 8k .. +7
       uint32_t w[4];
-      lds128(vb + swz128(r, (q & 1) * 4 + k), w[0], w[1], w[2], w[3]);
+      lds128(vb + Lay<true>::f(r, 4 * q + k), w[0], w[1], w[2], w[3]);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 f2 = __half22float2(u32_as_h2(w[e]));
@@ -615,13 +642,12 @@ __device__ __forceinline__ void quantize_flushed_group(const KParams& p, int64_t
       }
     }
   } else {
-    const __half* krow = p.k_res + (unit * C + s0) * kHeadDim + c;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = __half2float(krow[j * kHeadDim]);
-    const uint4* vrow = reinterpret_cast<const uint4*>(p.v_res + (unit * C + s0 + tok) * kHeadDim + q * 32);
+    for (int j = 0; j < 32; ++j) x[j] = __half2float(p.k_res[(unit * C + s0 + j) * kHeadDim + res_elem(s0 + j, c)]);
+    const uint4* vrow = reinterpret_cast<const uint4*>(p.v_res + (unit * C + s0 + tok) * kHeadDim);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const uint4 v = vrow[k];
+      const uint4 v = vrow[res_chunk(s0 + tok, 4 * q + k)];
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -631,16 +657,14 @@ __device__ __forceinline__ void quantize_flushed_group(const KParams& p, int64_t
       }
     }
   }
-  const int64_t g = unit * p.n_groups + gs;
-  store_group_record(x, y, qs, sl, const_cast<uint8_t*>(p.kw_p) + g * 1024, const_cast<__half*>(p.kw_s) + g * 128,
-                     const_cast<__half*>(p.kw_z) + g * 128, const_cast<uint8_t*>(p.vw_p) + g * 1024,
-                     const_cast<__half*>(p.vw_s) + g * 128, const_cast<__half*>(p.vw_z) + g * 128, c);
+  store_group_record(x, y, qs, sl, group_rec(p.grp, unit, p.n_groups, 1 + gs), c);
 }
 
 // Load issue, run by lane 0 of warp 0.  Each ring is filled in order; an
 // item is issued once warp 0 itself has consumed the previous user of its
 // stage (the other warps' release is then waited for, which never depends on
 // an item not yet issued).
+template <bool kRec>
 struct Issuer {
   const KParams& p;
   Smem& sm;
@@ -659,6 +683,13 @@ struct Issuer {
   __device__ __forceinline__ void batch(int b, uint32_t s) {
     const uint32_t fb = smem_u32(&sm.q_full[s]);
     const uint32_t sd = smem_u32(sm.qb[s]);
+    if constexpr (kRec) {  // batch slot v of the unit is its record v: one copy
+      const int v0 = kBatchGroups * b, v1 = min(p.n_groups + 1, v0 + kBatchGroups);
+      const uint32_t bytes = static_cast<uint32_t>(v1 - v0) * kRecBytes;
+      mbar_arrive_expect_tx(fb, bytes);
+      bulk_load(sd, p.grp + (unit * (p.n_groups + 1) + v0) * int64_t(kRecBytes), bytes, fb);
+      return;
+    }
     const int p0 = b == 0 ? 0 : kBatchGroups * b - 1;  // batch slot v holds group v - 1
     const int p1 = min(p.n_groups, kBatchGroups * b + kBatchGroups - 1);
     const int so = p0 + 1 - kBatchGroups * b;
@@ -697,10 +728,19 @@ struct Issuer {
       }
       const uint32_t fb = smem_u32(&sm.f_full[s]);
       const uint32_t sd = smem_u32(sm.f[s]);
-      mbar_arrive_expect_tx(fb, kFStageBytes);
-      const int uu = static_cast<int>(unit);
-      tma_load_4d(sd, tmK, fb, 0, f_next * kFRows, 0, uu);
-      tma_load_4d(sd + kFTile, tmV, fb, 0, f_next * kFRows, 0, uu);
+      if constexpr (kRec) {  // rows f_next*80 .. of the unit's ring, K and V one copy each
+        const int row0 = f_next * kFRows;
+        const uint32_t rows = static_cast<uint32_t>(min(kFRows, p.res_cap - row0));
+        mbar_arrive_expect_tx(fb, 2 * rows * 256);
+        const int64_t off = (unit * p.res_cap + row0) * kHeadDim;
+        bulk_load(sd, p.k_res + off, rows * 256, fb);
+        bulk_load(sd + kFTile, p.v_res + off, rows * 256, fb);
+      } else {
+        mbar_arrive_expect_tx(fb, kFStageBytes);
+        const int uu = static_cast<int>(unit);
+        tma_load_4d(sd, tmK, fb, 0, f_next * kFRows, 0, uu);
+        tma_load_4d(sd + kFTile, tmV, fb, 0, f_next * kFRows, 0, uu);
+      }
       ++f_issued;
       ++f_next;
     }
@@ -724,9 +764,10 @@ struct Issuer {
   }
 };
 
-// The work of CTA `bid` of one layer's launch (tensor maps and parameters in
-// kernel-parameter space).
-__device__ __forceinline__ void kivi_decode_cta(const CUtensorMap& tmK, const CUtensorMap& tmV, const KParams& p,
+// The work of CTA `bid` of one layer's launch (tensor maps -- reference
+// layout only -- and parameters in kernel-parameter space).
+template <bool kRec>
+__device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CUtensorMap* tmV, const KParams& p,
                                                 int64_t bid) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   grid_launch_dependents();
@@ -768,18 +809,20 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap& tmK, const CU
   const int ct = threadIdx.x;
   const uint4 qv = __ldg(reinterpret_cast<const uint4*>(p.q + (unit * kGroupHeads + (ct >> 4)) * kHeadDim +
                                                        (ct & 15) * 8));
-  const bool appending = p.new_k != nullptr;
+  const bool appending = kRec && p.new_k != nullptr;  // the reference layout never appends
   int64_t len = p.layout == 0 ? p.seq_len : p.unit_lens[unit];
   __half new_kc = __float2half_rn(0.f), new_vc = new_kc;
   if (appending) {
     new_kc = p.new_k[unit * kHeadDim + ct];
     new_vc = p.new_v[unit * kHeadDim + ct];
   }
-  Issuer iss(p, sm, &tmK, &tmV, unit, f_begin, f_end, b_begin, b_end);
+  Issuer<kRec> iss(p, sm, tmK, tmV, unit, f_begin, f_end, b_begin, b_end);
   const bool leader = threadIdx.x == 0;
   if (leader) {
-    prefetch_tmap(&tmK);
-    prefetch_tmap(&tmV);
+    if constexpr (!kRec) {
+      prefetch_tmap(tmK);
+      prefetch_tmap(tmV);
+    }
     if (has_b0) iss.batch0();
     iss.pump_f(0);
   }
@@ -854,14 +897,16 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap& tmK, const CU
 #pragma unroll
           for (int h = 0; h < 2; ++h)
             if (h == 0 || two)
-              zero_invalid_v_rows(sd + kFTile, kFRegion, r + 16 * h, vl[h] || ap.flushing(r0 + 16 * h + g),
-                                  vh[h] || ap.flushing(r0 + 16 * h + g + 8), lane);
+              zero_invalid_v_rows<kRec>(sd + kFTile, r + 16 * h, vl[h] || ap.flushing(r0 + 16 * h + g),
+                                        vh[h] || ap.flushing(r0 + 16 * h + g + 8), lane);
           if (two && any0 && any1) {
-            st.consume_rows<2>(sd, sd + kFTile, kFRegion, r, vl, vh, p.scale_log2, lane);
+            st.consume_rows<2, Lay<kRec>::kRowBytes>(sd, sd + kFTile, Lay<kRec>::kRegion, r, vl, vh, p.scale_log2,
+                                                     lane);
           } else {
             const int h = any0 ? 0 : 1;
             const bool l1[1] = {vl[h]}, h1[1] = {vh[h]};
-            st.consume_rows<1>(sd, sd + kFTile, kFRegion, r + 16 * h, l1, h1, p.scale_log2, lane);
+            st.consume_rows<1, Lay<kRec>::kRowBytes>(sd, sd + kFTile, Lay<kRec>::kRegion, r + 16 * h, l1, h1,
+                                                     p.scale_log2, lane);
           }
         }
         __syncwarp();
@@ -874,7 +919,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap& tmK, const CU
         const uint32_t mask = group_mask(p, meta, 0, ap.fl_slot);
         const int halves = ((mask & 0xffffu) ? 1 : 0) + ((mask >> 16) ? 1 : 0);
         if (mask && js.take(kCostGroup + kCostGroupHalf * halves) == warp)
-          attend_group(st, qrow, lq, qs, ap.fl_slot, mask, p.scale_log2, lane);
+          attend_group<kRec>(st, qrow, lq, qs, ap.fl_slot, mask, p.scale_log2, lane);
       }
       continue;
     }
@@ -910,7 +955,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap& tmK, const CU
         if (!mask || (defer_slot && b == 0 && gs == ap.fl_slot)) continue;
         const int halves = ((mask & 0xffffu) ? 1 : 0) + ((mask >> 16) ? 1 : 0);
         if (js.take(kCostGroup + kCostGroupHalf * halves) != warp) continue;
-        attend_group(st, qrow, lq, qs, gs, mask, p.scale_log2, lane);
+        attend_group<kRec>(st, qrow, lq, qs, gs, mask, p.scale_log2, lane);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&sm.q_empty[s]));
@@ -932,9 +977,9 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap& tmK, const CU
   }
   if (appending) {
     if (ap.f_item >= 0) {  // the new token's residual slot
-      const int64_t slot = (len - 1 - p.sink) % p.res_cap;
-      p.k_res[(unit * p.res_cap + slot) * kHeadDim + ct] = new_kc;
-      p.v_res[(unit * p.res_cap + slot) * kHeadDim + ct] = new_vc;
+      const int slot = static_cast<int>((len - 1 - p.sink) % p.res_cap);
+      p.k_res[(unit * p.res_cap + slot) * kHeadDim + res_elem(slot, ct)] = new_kc;
+      p.v_res[(unit * p.res_cap + slot) * kHeadDim + res_elem(slot, ct)] = new_vc;
     }
     if (ct == 0) p.unit_lens[unit] = len;  // every thread read the old length at entry
   }
@@ -963,10 +1008,16 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap& tmK, const CU
   }
 }
 
+// The reference's 14-tensor layout (residual by TMA boxes).
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     kivi_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                        const KParams p) {
-  kivi_decode_cta(tmK, tmV, p, blockIdx.x);
+  kivi_decode_cta<false>(&tmK, &tmV, p, blockIdx.x);
+}
+
+// The streaming cache (every load a 1-D bulk copy).
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) kivi_stream_decode_kernel(const KParams p) {
+  kivi_decode_cta<true>(nullptr, nullptr, p, blockIdx.x);
 }
 
 // Several layers (caches of one geometry) in one launch: layer-major CTAs,
@@ -975,8 +1026,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 // layer's query at once.
 constexpr int kMaxLayers = 24;
 struct KiviLayers {
-  CUtensorMap tmK[kMaxLayers];
-  CUtensorMap tmV[kMaxLayers];
   KParams p[kMaxLayers];
   int64_t per_layer;
   int n_layers;
@@ -985,7 +1034,7 @@ static_assert(sizeof(KiviLayers) <= 32000, "kernel parameter space");
 
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) kivi_decode_layers_kernel(const __grid_constant__ KiviLayers L) {
   const int layer = static_cast<int>(blockIdx.x / L.per_layer);
-  kivi_decode_cta(L.tmK[layer], L.tmV[layer], L.p[layer], blockIdx.x % L.per_layer);
+  kivi_decode_cta<true>(nullptr, nullptr, L.p[layer], blockIdx.x % L.per_layer);
 }
 
 struct Plan {
@@ -1004,6 +1053,8 @@ int64_t cta_slots() {
   if (!slots[dev]) {
     int per_sm = 0;
     if (cudaFuncSetAttribute(kivi_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(kivi_stream_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(kivi_decode_layers_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemBytes)) != cudaSuccess ||
@@ -1041,10 +1092,10 @@ size_t ws_bytes(const Plan& s) {
   return counters + lse + pieces * kGroupHeads * kHeadDim * sizeof(float);
 }
 
-// Completes p for plan s (workspace carving, device error word) and encodes
-// the residual tensor maps.
-int prepare(KParams& p, const Plan& s, const void* k_res, const void* v_res, void* ws, size_t wsb, CUtensorMap& mk,
-            CUtensorMap& mv) {
+// Completes p for plan s (workspace carving, device error word) and, for the
+// reference layout, encodes the residual tensor maps.
+int prepare(KParams& p, const Plan& s, const void* k_res, const void* v_res, void* ws, size_t wsb, CUtensorMap* mk,
+            CUtensorMap* mv) {
   const size_t need = ws_bytes(s);
   if (!ws || wsb < need)
     return fail(NSA_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, ws ? wsb : size_t(0));
@@ -1064,28 +1115,31 @@ int prepare(KParams& p, const Plan& s, const void* k_res, const void* v_res, voi
   p.ppu = s.ppu;
   p.err = device_error_word();
   if (!p.err) return fail(NSA_ERR_CUDA, "device error word unavailable");
+  if (p.layout != 0) return NSA_OK;
   // residual [units][res_cap][128] viewed as [units][2 halves][res_cap][64] (dims
   // innermost first): one box brings 80 slots x both 64-dim halves, each half a
   // 128-byte-swizzled region of 80 rows
   const uint64_t dims[4] = {64, static_cast<uint64_t>(p.res_cap), 2, static_cast<uint64_t>(s.n_units)};
   const uint64_t strides[3] = {kHeadDim * 2, 128, static_cast<uint64_t>(p.res_cap) * kHeadDim * 2};
   const uint32_t box[4] = {64, kFRows, 2, 1};
-  int rc = encode_tiled(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, k_res, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  int rc = encode_tiled(mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, k_res, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  return encode_tiled(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, v_res, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  return encode_tiled(mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, v_res, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 int launch(KParams& p, const Plan& s, const void* k_res, const void* v_res, void* ws, size_t wsb,
            cudaStream_t stream) {
   if (s.n_units == 0) return NSA_OK;
   CUtensorMap mk, mv;
-  int rc = prepare(p, s, k_res, v_res, ws, wsb, mk, mv);
+  int rc = prepare(p, s, k_res, v_res, ws, wsb, &mk, &mv);
   if (rc) return rc;
   cta_slots();  // sets the shared-memory limit
-  cudaError_t e = launch_kernel(kivi_decode_kernel, dim3(static_cast<unsigned>(s.grid)), dim3(kThreads), kSmemBytes,
-                                stream, mk, mv, p);
+  cudaError_t e = p.layout == 0 ? launch_kernel(kivi_decode_kernel, dim3(static_cast<unsigned>(s.grid)),
+                                                dim3(kThreads), kSmemBytes, stream, mk, mv, p)
+                                : launch_kernel(kivi_stream_decode_kernel, dim3(static_cast<unsigned>(s.grid)),
+                                                dim3(kThreads), kSmemBytes, stream, p);
   if (e == cudaSuccess) e = cudaGetLastError();
-  return e == cudaSuccess ? NSA_OK : cuda_fail(e, "kivi_decode_kernel launch");
+  return e == cudaSuccess ? NSA_OK : cuda_fail(e, "kivi decode launch");
 }
 
 bool all_aligned(std::initializer_list<const void*> ptrs) {
@@ -1106,12 +1160,8 @@ int kivi_check_stream_cache(const nsa_kivi_stream_cache& c) {
   const int64_t ng = c.window >= c.residual ? (c.window - c.residual) / 32 : 0;
   if (c.n_groups != ng) return fail(NSA_ERR_INVALID, "n_groups must be (window - residual) / 32");
   if (!c.unit_lens) return fail(NSA_ERR_INVALID, "unit_lens must not be NULL");
-  if (!all_aligned({c.sink_k, c.sink_v, c.k_sink_packed, c.k_sink_scale, c.k_sink_zero, c.v_sink_packed,
-                    c.v_sink_scale, c.v_sink_zero, c.k_res, c.v_res}))
+  if (!all_aligned({c.sink_k, c.sink_v, c.groups, c.k_res, c.v_res}))
     return fail(NSA_ERR_ALIGN, "stream cache tensors must be non-null and 16-byte aligned");
-  if (ng > 0 && !all_aligned({c.k_win_packed, c.k_win_scale, c.k_win_zero, c.v_win_packed, c.v_win_scale,
-                              c.v_win_zero}))
-    return fail(NSA_ERR_ALIGN, "window tensors must be non-null and 16-byte aligned");
   return NSA_OK;
 }
 
@@ -1198,18 +1248,9 @@ void stream_params(const nsa_kivi_stream_cache& c, const void* q, void* o, float
   p.n_groups = static_cast<int>(c.n_groups);
   p.res_cap = static_cast<int>(c.residual + 32);
   p.scale_log2 = sm_scale * 1.4426950408889634f;
-  p.ks_p = static_cast<const uint8_t*>(c.k_sink_packed);
-  p.ks_s = static_cast<const __half*>(c.k_sink_scale);
-  p.ks_z = static_cast<const __half*>(c.k_sink_zero);
-  p.vs_p = static_cast<const uint8_t*>(c.v_sink_packed);
-  p.vs_s = static_cast<const __half*>(c.v_sink_scale);
-  p.vs_z = static_cast<const __half*>(c.v_sink_zero);
-  p.kw_p = static_cast<const uint8_t*>(c.k_win_packed);
-  p.kw_s = static_cast<const __half*>(c.k_win_scale);
-  p.kw_z = static_cast<const __half*>(c.k_win_zero);
-  p.vw_p = static_cast<const uint8_t*>(c.v_win_packed);
-  p.vw_s = static_cast<const __half*>(c.v_win_scale);
-  p.vw_z = static_cast<const __half*>(c.v_win_zero);
+  p.grp = static_cast<uint8_t*>(c.groups);
+  p.k_res = static_cast<__half*>(c.k_res);
+  p.v_res = static_cast<__half*>(c.v_res);
 }
 
 // Whether a decode step may append inside the attention launch (NSA_FUSED_APPEND=0
@@ -1257,8 +1298,6 @@ int nsa_kivi_stream_decode_step(const nsa_kivi_stream_cache* cache, const void* 
     stream_params(c, q, o, sm_scale, p);
     p.new_k = static_cast<const __half*>(new_k);
     p.new_v = static_cast<const __half*>(new_v);
-    p.k_res = static_cast<__half*>(c.k_res);
-    p.v_res = static_cast<__half*>(c.v_res);
     p.sink_k16 = static_cast<__half*>(c.sink_k);
     p.sink_v16 = static_cast<__half*>(c.sink_v);
     return launch(p, s, c.k_res, c.v_res, workspace, workspace_bytes, stream);
@@ -1298,7 +1337,7 @@ int nsa_kivi_stream_decode_step_layers(const nsa_kivi_stream_cache* caches, int6
     }
     return NSA_OK;
   }
-  static thread_local KiviLayers L;  // ~19 KB: kept off the stack
+  static thread_local KiviLayers L;  // kept off the stack
   cta_slots();
   for (int64_t l0 = 0; l0 < n_layers; l0 += kMaxLayers) {
     const int n = static_cast<int>(n_layers - l0 < kMaxLayers ? n_layers - l0 : kMaxLayers);
@@ -1308,11 +1347,9 @@ int nsa_kivi_stream_decode_step_layers(const nsa_kivi_stream_cache* caches, int6
       stream_params(c, q[l0 + i], o[l0 + i], sm_scale, p);
       p.new_k = static_cast<const __half*>(new_k[l0 + i]);
       p.new_v = static_cast<const __half*>(new_v[l0 + i]);
-      p.k_res = static_cast<__half*>(c.k_res);
-      p.v_res = static_cast<__half*>(c.v_res);
       p.sink_k16 = static_cast<__half*>(c.sink_k);
       p.sink_v16 = static_cast<__half*>(c.sink_v);
-      int rc = prepare(p, s, c.k_res, c.v_res, workspace, workspace_bytes, L.tmK[i], L.tmV[i]);
+      int rc = prepare(p, s, c.k_res, c.v_res, workspace, workspace_bytes, nullptr, nullptr);
       if (rc) return rc;
     }
     L.per_layer = s.grid;

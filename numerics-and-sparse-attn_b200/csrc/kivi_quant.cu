@@ -14,6 +14,7 @@
 #include <cuda_fp16.h>
 
 #include "common.cuh"
+#include "kivi_format.cuh"
 #include "quant_math.cuh"
 #include "host_util.h"
 
@@ -151,17 +152,12 @@ int grid_for(int64_t total, int threads) {
 }  // namespace
 
 // ---------------------------------------------------------------- append
-// Quantize-on-append for the streaming cache (layout in nsa_b200.h,
-// nsa_kivi_stream_cache).  One CTA of 128 threads (thread = channel) per
-// (batch, kv_head) unit; the unit's own length word orders everything, so no
-// CTA depends on another.
+// Quantize-on-append for the streaming cache (format in kivi_format.cuh).
+// One CTA of 128 threads (thread = channel) per (batch, kv_head) unit; the
+// unit's own length word orders everything, so no CTA depends on another.
 __global__ void kivi_append_kernel(const __half* __restrict__ new_k, const __half* __restrict__ new_v,
                                    __half* __restrict__ sink_k16, __half* __restrict__ sink_v16,
-                                   uint8_t* __restrict__ ks_p, __half* __restrict__ ks_s, __half* __restrict__ ks_z,
-                                   uint8_t* __restrict__ vs_p, __half* __restrict__ vs_s, __half* __restrict__ vs_z,
-                                   uint8_t* __restrict__ kw_p, __half* __restrict__ kw_s, __half* __restrict__ kw_z,
-                                   uint8_t* __restrict__ vw_p, __half* __restrict__ vw_s, __half* __restrict__ vw_z,
-                                   __half* __restrict__ k_res, __half* __restrict__ v_res,
+                                   uint8_t* __restrict__ grp, __half* __restrict__ k_res, __half* __restrict__ v_res,
                                    int64_t* __restrict__ unit_lens, int sink, int residual, int n_groups) {
   constexpr int D = 128;
   grid_launch_dependents();
@@ -173,95 +169,74 @@ __global__ void kivi_append_kernel(const __half* __restrict__ new_k, const __hal
   const __half kx = new_k[u * D + c];
   const __half vx = new_v[u * D + c];
   __shared__ float vbuf[32][D + 1];  // V rows of a flushed group (float32, padded)
+  GroupRec rec{};
+  float x[32];  // K of channel c over the group's 32 tokens
+  bool quantize = false;
 
   if (pos < sink) {
-    // sink token: keep an fp16 copy, re-quantize the padded sink group
+    // sink token: keep an fp16 copy, re-quantize the padded sink group (the n
+    // real tokens, then copies of token 0)
     sink_k16[(u * sink + pos) * D + c] = kx;
     sink_v16[(u * sink + pos) * D + c] = vx;
     __syncthreads();
     const int n = static_cast<int>(pos) + 1;
-    // K: per channel over 32 tokens = the n real ones + copies of token 0
-    float x[32];
+    for (int j = 0; j < 32; ++j) {
+      const int src = j < n ? j : 0;
+      x[j] = __half2float(sink_k16[(u * sink + src) * D + c]);
+      vbuf[j][c] = __half2float(sink_v16[(u * sink + src) * D + c]);
+    }
+    rec = group_rec(grp, u, n_groups, 0);
+    quantize = true;
+  } else {
+    const int64_t i = pos - sink;  // stream index
+    const int slot = static_cast<int>(i % cap);
+    k_res[(u * cap + slot) * D + res_elem(slot, c)] = kx;
+    v_res[(u * cap + slot) * D + res_elem(slot, c)] = vx;
+    const int64_t f_old = (i - residual) >= 0 ? (i - residual) / 32 : 0;  // flushed before this token
+    const int64_t f_new = (i + 1 - residual) >= 0 ? (i + 1 - residual) / 32 : 0;
+    if (f_new > f_old && n_groups > 0) {
+      // flush stream group f_old: indices [32 f_old, 32 f_old + 32) into window slot f_old % NG
+      __syncthreads();
+      const int64_t base = 32 * f_old;
+      for (int j = 0; j < 32; ++j) {
+        const int s = static_cast<int>((base + j) % cap);
+        x[j] = __half2float(k_res[(u * cap + s) * D + res_elem(s, c)]);
+        vbuf[j][c] = __half2float(v_res[(u * cap + s) * D + res_elem(s, c)]);
+      }
+      rec = group_rec(grp, u, n_groups, 1 + static_cast<int>(f_old % n_groups));
+      quantize = true;
+    }
+  }
+  if (quantize) {  // uniform across the CTA
+    __syncthreads();
+    // K: per channel over the 32 tokens
     float mn = INFINITY, mx = -INFINITY;
     for (int j = 0; j < 32; ++j) {
-      x[j] = __half2float(sink_k16[(u * sink + (j < n ? j : 0)) * D + c]);
       mn = fminf(mn, x[j]);
       mx = fmaxf(mx, x[j]);
     }
     GroupParams gp = group_params(mn, mx);
-    ks_s[u * D + c] = __float2half_rn(gp.scale);
-    ks_z[u * D + c] = __float2half_rn(gp.zero);
+    rec.ks[c] = __float2half_rn(gp.scale);
+    rec.kz[c] = __float2half_rn(gp.zero);
     for (int bq = 0; bq < 8; ++bq) {
       uint32_t byte = 0;
       for (int j = 0; j < 4; ++j) byte |= code_of(x[4 * bq + j], gp) << (2 * j);
-      ks_p[(u * 8 + bq) * D + c] = static_cast<uint8_t>(byte);
+      rec.kp[bq * D + c] = static_cast<uint8_t>(byte);
     }
-    // V: per token (32 padded tokens x 4 channel groups): thread = (token, group)
-    {
-      const int tok = c >> 2, q = c & 3;
-      const int src = tok < n ? tok : 0;
-      float y[32];
-      float vmn = INFINITY, vmx = -INFINITY;
-      for (int j = 0; j < 32; ++j) {
-        y[j] = __half2float(sink_v16[(u * sink + src) * D + q * 32 + j]);
-        vmn = fminf(vmn, y[j]);
-        vmx = fmaxf(vmx, y[j]);
-      }
-      gp = group_params(vmn, vmx);
-      vs_s[(u * 32 + tok) * 4 + q] = __float2half_rn(gp.scale);
-      vs_z[(u * 32 + tok) * 4 + q] = __float2half_rn(gp.zero);
-      uint32_t lo = 0, hi = 0;
-      for (int j = 0; j < 16; ++j) lo |= code_of(y[j], gp) << (2 * j);
-      for (int j = 0; j < 16; ++j) hi |= code_of(y[16 + j], gp) << (2 * j);
-      *reinterpret_cast<uint2*>(vs_p + (u * 32 + tok) * 32 + q * 8) = make_uint2(lo, hi);
+    // V: per token (32 tokens x 4 channel groups): thread = (token, group)
+    const int tok = c >> 2, q = c & 3;
+    float vmn = INFINITY, vmx = -INFINITY;
+    for (int j = 0; j < 32; ++j) {
+      vmn = fminf(vmn, vbuf[tok][q * 32 + j]);
+      vmx = fmaxf(vmx, vbuf[tok][q * 32 + j]);
     }
-  } else {
-    const int64_t i = pos - sink;  // stream index
-    const int slot = static_cast<int>(i % cap);
-    k_res[(u * cap + slot) * D + c] = kx;
-    v_res[(u * cap + slot) * D + c] = vx;
-    const int64_t f_old = (i - residual) >= 0 ? (i - residual) / 32 : 0;   // flushed before this token
-    const int64_t f_new = (i + 1 - residual) >= 0 ? (i + 1 - residual) / 32 : 0;
-    if (f_new > f_old) {
-      // flush stream group f_old: indices [32 f_old, 32 f_old + 32)
-      __syncthreads();
-      const int64_t base = 32 * f_old;
-      const int gs = n_groups > 0 ? static_cast<int>(f_old % n_groups) : -1;
-      float x[32];
-      float mn = INFINITY, mx = -INFINITY;
-      for (int j = 0; j < 32; ++j) {
-        const int s = static_cast<int>((base + j) % cap);
-        x[j] = __half2float(k_res[(u * cap + s) * D + c]);
-        mn = fminf(mn, x[j]);
-        mx = fmaxf(mx, x[j]);
-        vbuf[j][c] = __half2float(v_res[(u * cap + s) * D + c]);
-      }
-      __syncthreads();
-      if (gs >= 0) {
-        GroupParams gp = group_params(mn, mx);
-        kw_s[(u * n_groups + gs) * D + c] = __float2half_rn(gp.scale);
-        kw_z[(u * n_groups + gs) * D + c] = __float2half_rn(gp.zero);
-        for (int bq = 0; bq < 8; ++bq) {
-          uint32_t byte = 0;
-          for (int j = 0; j < 4; ++j) byte |= code_of(x[4 * bq + j], gp) << (2 * j);
-          kw_p[((u * n_groups + gs) * 8 + bq) * D + c] = static_cast<uint8_t>(byte);
-        }
-        const int tok = c >> 2, q = c & 3;
-        float vmn = INFINITY, vmx = -INFINITY;
-        for (int j = 0; j < 32; ++j) {
-          vmn = fminf(vmn, vbuf[tok][q * 32 + j]);
-          vmx = fmaxf(vmx, vbuf[tok][q * 32 + j]);
-        }
-        gp = group_params(vmn, vmx);
-        const int64_t row = (u * n_groups + gs) * 32 + tok;
-        vw_s[row * 4 + q] = __float2half_rn(gp.scale);
-        vw_z[row * 4 + q] = __float2half_rn(gp.zero);
-        uint32_t lo = 0, hi = 0;
-        for (int j = 0; j < 16; ++j) lo |= code_of(vbuf[tok][q * 32 + j], gp) << (2 * j);
-        for (int j = 0; j < 16; ++j) hi |= code_of(vbuf[tok][q * 32 + 16 + j], gp) << (2 * j);
-        *reinterpret_cast<uint2*>(vw_p + row * 32 + q * 8) = make_uint2(lo, hi);
-      }
-    }
+    gp = group_params(vmn, vmx);
+    rec.vs[tok * 4 + q] = __float2half_rn(gp.scale);
+    rec.vz[tok * 4 + q] = __float2half_rn(gp.zero);
+    uint32_t lo = 0, hi = 0;
+    for (int j = 0; j < 16; ++j) lo |= code_of(vbuf[tok][q * 32 + j], gp) << (2 * j);
+    for (int j = 0; j < 16; ++j) hi |= code_of(vbuf[tok][q * 32 + 16 + j], gp) << (2 * j);
+    *reinterpret_cast<uint2*>(rec.vp + tok * 32 + q * 8) = make_uint2(lo, hi);
   }
   __syncthreads();  // every thread has read the length
   if (c == 0) unit_lens[u] = pos + 1;
@@ -379,13 +354,9 @@ int nsa_kivi_append(const nsa_kivi_stream_cache* cache, const void* new_k, const
   cudaError_t e = launch_kernel(
       kivi_append_kernel, dim3(static_cast<unsigned>(units)), dim3(128), 0, stream,
       static_cast<const __half*>(new_k), static_cast<const __half*>(new_v), static_cast<__half*>(c.sink_k),
-      static_cast<__half*>(c.sink_v), static_cast<uint8_t*>(c.k_sink_packed), static_cast<__half*>(c.k_sink_scale),
-      static_cast<__half*>(c.k_sink_zero), static_cast<uint8_t*>(c.v_sink_packed),
-      static_cast<__half*>(c.v_sink_scale), static_cast<__half*>(c.v_sink_zero),
-      static_cast<uint8_t*>(c.k_win_packed), static_cast<__half*>(c.k_win_scale), static_cast<__half*>(c.k_win_zero),
-      static_cast<uint8_t*>(c.v_win_packed), static_cast<__half*>(c.v_win_scale), static_cast<__half*>(c.v_win_zero),
-      static_cast<__half*>(c.k_res), static_cast<__half*>(c.v_res), c.unit_lens, static_cast<int>(c.sink),
-      static_cast<int>(c.residual), static_cast<int>(c.n_groups));
+      static_cast<__half*>(c.sink_v), static_cast<uint8_t*>(c.groups), static_cast<__half*>(c.k_res),
+      static_cast<__half*>(c.v_res), c.unit_lens, static_cast<int>(c.sink), static_cast<int>(c.residual),
+      static_cast<int>(c.n_groups));
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? NSA_OK : cuda_fail(e, "kivi_append launch");
 }

@@ -191,11 +191,44 @@ class KiviStreamCacheDesc(ctypes.Structure):
     """ctypes mirror of nsa_kivi_stream_cache (include/nsa_b200.h)."""
     _fields_ = [(n, ctypes.c_int64) for n in ("batch", "n_kv_heads", "head_dim", "window", "sink", "residual",
                                               "n_groups")] + \
-               [(n, ctypes.c_void_p) for n in ("unit_lens", "sink_k", "sink_v",
-                                               "k_sink_packed", "k_sink_scale", "k_sink_zero",
-                                               "v_sink_packed", "v_sink_scale", "v_sink_zero",
-                                               "k_win_packed", "k_win_scale", "k_win_zero",
-                                               "v_win_packed", "v_win_scale", "v_win_zero", "k_res", "v_res")]
+               [(n, ctypes.c_void_p) for n in ("unit_lens", "sink_k", "sink_v", "groups", "k_res", "v_res")]
+
+
+# Group records of the streaming cache (csrc/kivi_format.cuh): one group's
+# share of the reference's six quantized tensors, 3 KiB.
+REC_BYTES = 3072
+_QUANT_NAMES = ("k_{}_packed", "k_{}_scale", "k_{}_zero", "v_{}_packed", "v_{}_scale", "v_{}_zero")
+
+
+def _record(kp, ks, kz, vp, vs, vz):
+    """Records u8 [..., 3072] from one group's tensors in the reference layouts
+    (kp u8 [..., 8, D], ks / kz f16 [..., 1, D], vp u8 [..., 32, D/4],
+    vs / vz f16 [..., 32, D/32])."""
+    lead = kp.shape[:-2]
+    return torch.cat([t.contiguous().view(torch.uint8).reshape(*lead, -1) for t in (kp, ks, kz, vp, vs, vz)], dim=-1)
+
+
+def _unrecord(rec):
+    """Records u8 [..., n, 3072] -> the six tensors in the reference layouts,
+    the n groups one after another along the token axis (copies)."""
+    lead, n = rec.shape[:-2], rec.shape[-2]
+
+    def f16(a, b, rows, cols):
+        return rec[..., a:b].contiguous().view(torch.float16).reshape(*lead, rows, cols)
+
+    return (rec[..., 0:1024].reshape(*lead, n * 8, D_HEAD), f16(1024, 1280, n, D_HEAD), f16(1280, 1536, n, D_HEAD),
+            rec[..., 1536:2560].reshape(*lead, n * GROUP_SIZE, D_HEAD // 4),
+            f16(2560, 2816, n * GROUP_SIZE, D_HEAD // 32), f16(2816, 3072, n * GROUP_SIZE, D_HEAD // 32))
+
+
+def _res_perm(n_slots, device):
+    """[n_slots, D] element order of the residual ring: slot s stores channel
+    c at perm[s, c], and perm[s] is its own inverse (16-byte chunk ch of the
+    row sits at chunk (ch & 8) | ((ch & 7) ^ (s & 7)))."""
+    s = torch.arange(n_slots, device=device)[:, None]
+    c = torch.arange(D_HEAD, device=device)[None, :]
+    ch = c >> 3
+    return (((ch & 8) | ((ch & 7) ^ (s & 7))) << 3) | (c & 7)
 
 
 def decode_step_layers(caches, qs, new_ks, new_vs, sm_scale=None):
@@ -256,15 +289,11 @@ class KiviCache:
 
         self.unit_lens = z((b, h), torch.int64)
         self.sink_k, self.sink_v = z((b, h, sink, d), f16), z((b, h, sink, d), f16)
-        self.k_sink_packed, self.k_sink_scale, self.k_sink_zero = z((b, h, 8, d), u8), z((b, h, 1, d), f16), \
-            z((b, h, 1, d), f16)
-        self.v_sink_packed, self.v_sink_scale, self.v_sink_zero = z((b, h, 32, d // 4), u8), \
-            z((b, h, 32, d // 32), f16), z((b, h, 32, d // 32), f16)
-        self.k_win_packed, self.k_win_scale, self.k_win_zero = z((b, h, ng * 8, d), u8), z((b, h, ng, d), f16), \
-            z((b, h, ng, d), f16)
-        self.v_win_packed, self.v_win_scale, self.v_win_zero = z((b, h, ng * 32, d // 4), u8), \
-            z((b, h, ng * 32, d // 32), f16), z((b, h, ng * 32, d // 32), f16)
+        # record 0: the sink group; record 1 + s: window-group slot s
+        self.groups = z((b, h, 1 + ng, REC_BYTES), u8)
+        # residual ring, slots chunk-permuted (_res_perm)
         self.k_res, self.v_res = z((b, h, self.res_cap, d), f16), z((b, h, self.res_cap, d), f16)
+        self._perm = _res_perm(self.res_cap, device)
         self._desc = self._make_desc()
         lib = _lib.load()
         self._ws_bytes = lib.nsa_kivi_stream_workspace_bytes(ctypes.byref(self._desc))
@@ -274,19 +303,25 @@ class KiviCache:
         dsc = KiviStreamCacheDesc()
         for n in ("batch", "n_kv_heads", "head_dim", "window", "sink", "residual", "n_groups"):
             setattr(dsc, n, int(getattr(self, n)))
-        for n in ("unit_lens", "sink_k", "sink_v", "k_sink_packed", "k_sink_scale", "k_sink_zero", "v_sink_packed",
-                  "v_sink_scale", "v_sink_zero", "k_win_packed", "k_win_scale", "k_win_zero", "v_win_packed",
-                  "v_win_scale", "v_win_zero", "k_res", "v_res"):
-            t = getattr(self, n)
-            setattr(dsc, n, t.data_ptr() if t.numel() else None)
+        for n in ("unit_lens", "sink_k", "sink_v", "groups", "k_res", "v_res"):
+            setattr(dsc, n, getattr(self, n).data_ptr())
         return dsc
 
+    def _logical_rows(self, t):
+        """Residual ring in channel order (copy)."""
+        return t.gather(-1, self._perm.expand_as(t))
+
     def state(self) -> dict:
-        """The cache tensors (views, not copies)."""
-        return {n: getattr(self, n) for n in ("unit_lens", "sink_k", "sink_v", "k_sink_packed", "k_sink_scale",
-                                              "k_sink_zero", "v_sink_packed", "v_sink_scale", "v_sink_zero",
-                                              "k_win_packed", "k_win_scale", "k_win_zero", "v_win_packed",
-                                              "v_win_scale", "v_win_zero", "k_res", "v_res")}
+        """The cache in the reference's tensor layouts (copies): unit_lens,
+        sink_k / sink_v, k_/v_{sink,win}_{packed,scale,zero} as
+        build_quantized_kv_cache lays them out (window groups in slot order),
+        and k_res / v_res [B, Hkv, R + 32, D] in channel order."""
+        st = {"unit_lens": self.unit_lens.clone(), "sink_k": self.sink_k.clone(), "sink_v": self.sink_v.clone()}
+        for where, recs in (("sink", self.groups[:, :, :1]), ("win", self.groups[:, :, 1:])):
+            for name, t in zip(_QUANT_NAMES, _unrecord(recs)):
+                st[name.format(where)] = t
+        st["k_res"], st["v_res"] = self._logical_rows(self.k_res), self._logical_rows(self.v_res)
+        return st
 
     @property
     def seq_len(self) -> int:
@@ -378,8 +413,7 @@ class KiviCache:
             self.sink_v[:, :, :ns] = vv
             kp = torch.cat([kk, kk[:, :, :1].expand(-1, -1, G - ns, -1)], dim=2).contiguous()
             vp = torch.cat([vv, vv[:, :, :1].expand(-1, -1, G - ns, -1)], dim=2).contiguous()
-            self.k_sink_packed[:], self.k_sink_scale[:], self.k_sink_zero[:] = quantize_k_cache(kp)
-            self.v_sink_packed[:], self.v_sink_scale[:], self.v_sink_zero[:] = quantize_v_cache(vp)
+            self.groups[:, :, 0] = _record(*quantize_k_cache(kp), *quantize_v_cache(vp))
 
         def tok(a, b):
             _req(tail_k is not None and a >= tail_start and b <= tail_start + tail_k.shape[2],
@@ -393,17 +427,15 @@ class KiviCache:
             vp, vs, vz = quantize_v_cache(vv.contiguous())
             for j in range(n_grp):
                 slot = (g0 + j) % NG
-                self.k_win_packed[:, :, slot * 8:(slot + 1) * 8] = kp[:, :, j * 8:(j + 1) * 8]
-                self.k_win_scale[:, :, slot] = ks[:, :, j]
-                self.k_win_zero[:, :, slot] = kz[:, :, j]
-                self.v_win_packed[:, :, slot * G:(slot + 1) * G] = vp[:, :, j * G:(j + 1) * G]
-                self.v_win_scale[:, :, slot * G:(slot + 1) * G] = vs[:, :, j * G:(j + 1) * G]
-                self.v_win_zero[:, :, slot * G:(slot + 1) * G] = vz[:, :, j * G:(j + 1) * G]
+                t, v = slice(j * G, (j + 1) * G), slice(j, j + 1)
+                self.groups[:, :, 1 + slot] = _record(kp[:, :, j * 8:(j + 1) * 8], ks[:, :, v], kz[:, :, v],
+                                                      vp[:, :, t], vs[:, :, t], vz[:, :, t])
         if n_stream > G * F:
             kk, vv = tok(S + G * F, seq_len)
             idx = torch.arange(G * F, n_stream, device=self.device) % C
-            self.k_res[:, :, idx] = kk
-            self.v_res[:, :, idx] = vv
+            perm = self._perm[idx].expand_as(kk)
+            self.k_res[:, :, idx] = kk.gather(-1, perm)
+            self.v_res[:, :, idx] = vv.gather(-1, perm)
 
     def load_history(self, k_hist, v_hist, seq_len):
         """State after appending positions [0, seq_len) of k_hist/v_hist
