@@ -65,6 +65,7 @@ constexpr uint32_t kFTile = 2 * kFRegion;    // K (or V) of one F-tile: one TMA 
 constexpr uint32_t kFStageBytes = 2 * kFTile;  // 40 KiB
 constexpr int kFStages = 2;
 constexpr int kQStages = 2;
+constexpr int64_t kMaxUnitLen = int64_t(1) << 30;  // longest unit the kernels accept
 constexpr int kBatchGroups = 5;            // quantized groups per Q-batch
 constexpr int kQPadStride = kHeadDim + 8;  // 272-byte rows: 8 rows of an ldmatrix hit distinct banks
 // Q-batch stage layout (byte offsets); one slot per group
@@ -174,33 +175,35 @@ __device__ __forceinline__ int32_t clampi(int64_t x, int64_t lo, int64_t hi) {
 // Per-unit metadata from the unit's length (see nsa_kivi_stream_cache and
 // _kv_indices, sparse_kernel.py:15-46, for the two layouts); `len` is the
 // streaming unit's length (unused for the reference layout).
-__device__ __forceinline__ KiviMeta make_meta(const KParams& p, int64_t len_stream) {
+template <bool kRec>
+__device__ __forceinline__ KiviMeta make_meta(const KParams& p, int len_stream) {
+  // 32-bit arithmetic: lengths stay below kMaxUnitLen (checked where read)
   KiviMeta m;
-  const int64_t S = p.sink, W = p.window, R = p.residual, NG = p.n_groups;
-  if (p.layout == 0) {
-    const int64_t len = p.seq_len;
-    const int64_t nw = W - R;  // window-old tokens
-    const int64_t n_inv = clampi(S - len + W, 0, W);  // window indices < n_inv are not attended
-    m.n_sink = clampi(len, 0, S);
+  const int S = p.sink, W = p.window, R = p.residual, NG = p.n_groups;
+  if constexpr (!kRec) {
+    const int len = static_cast<int>(p.seq_len);  // the host caps it at kMaxUnitLen
+    const int nw = W - R;                          // window-old tokens
+    const int n_inv = min(max(S - len + W, 0), W);  // window indices < n_inv are not attended
+    m.n_sink = min(max(len, 0), S);
     m.grp_head = 0;
-    m.n_grp = static_cast<int32_t>(NG);
-    m.tok_skip = clampi(n_inv, 0, nw);
+    m.n_grp = NG;
+    m.tok_skip = min(n_inv, nw);
     m.res_head = 0;
-    m.n_res = static_cast<int32_t>(R);
-    m.res_skip = clampi(n_inv - nw, 0, R);
+    m.n_res = R;
+    m.res_skip = min(max(n_inv - nw, 0), R);
   } else {
-    const int64_t len = len_stream;
-    const int64_t C = p.res_cap;
-    const int64_t n_stream = len > S ? len - S : 0;
-    const int64_t F = n_stream > R ? (n_stream - R) / 32 : 0;  // flushed groups
-    const int64_t first = (len - W > S) ? len - W : S;         // oldest attended position
-    m.n_sink = clampi(len, 0, S);
-    m.n_res = static_cast<int32_t>(n_stream - 32 * F);
-    m.res_head = static_cast<int32_t>((32 * F) % C);
-    m.res_skip = clampi(first - S - 32 * F, 0, m.n_res);
-    m.n_grp = static_cast<int32_t>(F < NG ? F : NG);
-    m.grp_head = NG > 0 ? static_cast<int32_t>((F - m.n_grp) % NG) : 0;
-    m.tok_skip = clampi(first - S - 32 * (F - m.n_grp), 0, 32 * int64_t(m.n_grp));
+    const int len = len_stream;
+    const int C = p.res_cap;
+    const int n_stream = len > S ? len - S : 0;
+    const int F = n_stream > R ? (n_stream - R) >> 5 : 0;  // flushed groups
+    const int first = max(len - W, S);                     // oldest attended position
+    m.n_sink = min(len, S);
+    m.n_res = n_stream - 32 * F;
+    m.res_head = (32 * F) % C;
+    m.res_skip = min(max(first - S - 32 * F, 0), m.n_res);
+    m.n_grp = min(F, NG);
+    m.grp_head = NG > 0 ? (F - m.n_grp) % NG : 0;
+    m.tok_skip = min(max(first - S - 32 * (F - m.n_grp), 0), 32 * m.n_grp);
   }
   m.pad = 0;
   return m;
@@ -502,7 +505,7 @@ struct AppendPlan {
   int fl_batch = -1;    // Q-batch and batch slot of the window group this append flushes (-1: none)
   int fl_slot = 0;
   int fl_gs = 0;        // its window-group slot
-  int64_t fl_base = 0;  // stream index of its first token
+  int fl_base = 0;      // stream index of its first token
   int fl_s0 = -1;       // its first residual slot (-1: no flush)
   __device__ __forceinline__ bool flushing(int slot) const { return fl_s0 >= 0 && slot >= fl_s0 && slot < fl_s0 + 32; }
 };
@@ -510,25 +513,24 @@ struct AppendPlan {
 // Where the append lands; pos = the unit's length before the append.  (The
 // token's own stores wait until its value is needed, so that no thread
 // stalls on its load early in the launch.)
-__device__ __forceinline__ AppendPlan append_plan(const KParams& p, int64_t pos) {
+__device__ __forceinline__ AppendPlan append_plan(const KParams& p, int pos) {
   AppendPlan a;
   const int S = p.sink, R = p.residual, C = p.res_cap, NG = p.n_groups;
   if (pos < S) {
     a.sink = true;
     return a;
   }
-  const int64_t i = pos - S;  // stream index
-  const int slot = static_cast<int>(i % C);
+  const int i = pos - S;  // stream index
+  const int slot = i % C;
   a.f_item = slot / kFRows;
   a.f_row = slot % kFRows;
-  const int64_t f_old = (i - R) >= 0 ? (i - R) / 32 : 0;  // groups flushed before this token
-  const int64_t f_new = (i + 1 - R) >= 0 ? (i + 1 - R) / 32 : 0;
-  if (f_new > f_old && NG > 0) {  // stream group f_old leaves the residual
-    a.fl_gs = static_cast<int>(f_old % NG);
+  if (i + 1 - R > 0 && ((i + 1 - R) & 31) == 0 && NG > 0) {  // stream group f_old leaves the residual
+    const int f_old = (i - R) >> 5;
+    a.fl_gs = f_old % NG;
     a.fl_base = 32 * f_old;
     a.fl_batch = (a.fl_gs + 1) / kBatchGroups;
     a.fl_slot = (a.fl_gs + 1) % kBatchGroups;
-    a.fl_s0 = static_cast<int>(a.fl_base % C);
+    a.fl_s0 = a.fl_base % C;
   }
   return a;
 }
@@ -596,7 +598,9 @@ __device__ __forceinline__ void store_group_record(const float (&x)[32], const f
 
 // The padded sink group of a unit holding n sink tokens (the n real ones,
 // then copies of token 0), into batch 0's slot 0 and the unit's record 0.
-__device__ __forceinline__ void requantize_sink(const KParams& p, int64_t unit, int n, uint32_t qs, int c) {
+// Out of line (with quantize_flushed_group): rare, and large once unrolled,
+// it would otherwise crowd the hot loop out of the instruction cache.
+__device__ __noinline__ void requantize_sink(const KParams& p, int64_t unit, int n, uint32_t qs, int c) {
   const int S = p.sink;
   float x[32], y[32];
 #pragma unroll
@@ -613,10 +617,10 @@ __device__ __forceinline__ void requantize_sink(const KParams& p, int64_t unit, 
 // `sl` and window-group slot gs.  Read from the staged F-tiles when every
 // F-tile of the unit is still resident (f_stage0: the F ring's base address),
 // else from the cache.
-__device__ __forceinline__ void quantize_flushed_group(const KParams& p, int64_t unit, int64_t base, int gs,
+__device__ __noinline__ void quantize_flushed_group(const KParams& p, int64_t unit, int base, int gs,
                                                        uint32_t qs, int sl, uint32_t f_stage0, int c) {
   const int C = p.res_cap;
-  const int s0 = static_cast<int>(base % C);
+  const int s0 = base % C;
   const int tok = c >> 2, q = c & 3;
   float x[32], y[32];
   if (f_stage0) {
@@ -765,10 +769,11 @@ struct Issuer {
 };
 
 // The work of CTA `bid` of one layer's launch (tensor maps -- reference
-// layout only -- and parameters in kernel-parameter space).
-template <bool kRec>
+// layout only -- and parameters in kernel-parameter space).  kAppend: the
+// launch also appends new_k / new_v (streaming layout, one CTA per unit).
+template <bool kRec, bool kAppend>
 __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CUtensorMap* tmV, const KParams& p,
-                                                int64_t bid) {
+                                                int bid) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   grid_launch_dependents();
   grid_dependency_wait();  // the cache and q may come from the previous kernel of the stream
@@ -779,7 +784,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t unit = bid / p.ppu;
-  const int piece = static_cast<int>(bid % p.ppu);
+  const int piece = bid % p.ppu;
   // this piece's items [t_begin, t_end): item 0 = Q-batch 0, items 1..n_ft =
   // F-tiles 0..n_ft-1, item n_ft + b = Q-batch b (b >= 1)
   const int t_begin = piece * p.items / p.ppu, t_end = (piece + 1) * p.items / p.ppu;
@@ -809,8 +814,9 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   const int ct = threadIdx.x;
   const uint4 qv = __ldg(reinterpret_cast<const uint4*>(p.q + (unit * kGroupHeads + (ct >> 4)) * kHeadDim +
                                                        (ct & 15) * 8));
-  const bool appending = kRec && p.new_k != nullptr;  // the reference layout never appends
-  int64_t len = p.layout == 0 ? p.seq_len : p.unit_lens[unit];
+  static_assert(kRec || !kAppend, "the reference layout never appends");
+  constexpr bool appending = kAppend;
+  const int64_t len64 = kRec ? p.unit_lens[unit] : 0;
   __half new_kc = __float2half_rn(0.f), new_vc = new_kc;
   if (appending) {
     new_kc = p.new_k[unit * kHeadDim + ct];
@@ -826,9 +832,14 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
     if (has_b0) iss.batch0();
     iss.pump_f(0);
   }
-  const AppendPlan ap = appending ? append_plan(p, len) : AppendPlan{};
-  if (appending) ++len;
-  const KiviMeta meta = make_meta(p, len);
+  int len = static_cast<int>(len64);
+  if (kRec && (len64 < 0 || len64 >= kMaxUnitLen)) {  // outside what the 32-bit ring arithmetic covers
+    if (threadIdx.x == 0) set_error(p.err, NSA_ERR_INVALID);
+    len = 0;
+  }
+  const AppendPlan ap = appending && len64 == len ? append_plan(p, len) : AppendPlan{};
+  if (appending && len64 == len) ++len;
+  const KiviMeta meta = make_meta<kRec>(p, len);
   if (leader) iss.pump_q(meta, 0);
   sts128(smem_u32(&sm.qpad[ct >> 4][(ct & 15) * 8]), qv.x, qv.y, qv.z, qv.w);
   if (appending) {
@@ -849,19 +860,21 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   const uint32_t qrow = qpad + g * (kQPadStride * 2) + 32 * t;
   JobSched js;
   uint32_t nf = 0, nq = 0;
-  // phase 0: Q-batch 0; phase 1: the F-tiles; phase 2: Q-batches b_begin ..
-  // (one loop so that each consumer path is instantiated once).  A group this
-  // launch flushes is quantized from the staged F-tiles after they have been
-  // consumed: when every item stays staged (resident), batch 0 keeps its place
-  // and only the flushed slot waits until after the F-tiles; otherwise the
+  // Steps: 0 = Q-batch 0, 1 = the F-tiles, 2 = Q-batches b_begin .., 3 = the
+  // deferred slot below (one loop, so that each consumer path -- attend_group
+  // above all -- is instantiated once).  A group this launch flushes is
+  // quantized from the staged F-tiles after they have been consumed: when
+  // every item stays staged (resident), batch 0 keeps its place and only the
+  // flushed slot waits until after the F-tiles (step 3); otherwise the
   // F-tiles come first and the group is read from the cache.
   const bool flushing = ap.fl_batch >= 0;
   const bool resident = p.n_qb <= kQStages && p.n_ft <= kFStages && f_begin == 0 && f_end == p.n_ft;
   const bool defer_slot = flushing && resident && ap.fl_batch == 0;
   const bool f_first = flushing && !resident;
 #pragma unroll 1
-  for (int step = 0; step < 3; ++step) {
+  for (int step = 0; step < 4; ++step) {
     const int phase = (f_first && step < 2) ? 1 - step : step;
+    if (phase == 3 && !defer_slot) break;
     if (phase == 1) {
 #pragma unroll 1
       for (int f = f_begin; f < f_end; ++f) {
@@ -903,62 +916,65 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
             st.consume_rows<2, Lay<kRec>::kRowBytes>(sd, sd + kFTile, Lay<kRec>::kRegion, r, vl, vh, p.scale_log2,
                                                      lane);
           } else {
-            const int h = any0 ? 0 : 1;
-            const bool l1[1] = {vl[h]}, h1[1] = {vh[h]};
-            st.consume_rows<1, Lay<kRec>::kRowBytes>(sd, sd + kFTile, Lay<kRec>::kRegion, r + 16 * h, l1, h1,
+            // (selects, not vl[h]: a dynamic index would put the flags in local memory)
+            const bool l1[1] = {any0 ? vl[0] : vl[1]}, h1[1] = {any0 ? vh[0] : vh[1]};
+            st.consume_rows<1, Lay<kRec>::kRowBytes>(sd, sd + kFTile, Lay<kRec>::kRegion, r + (any0 ? 0 : 16), l1, h1,
                                                      p.scale_log2, lane);
           }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&sm.f_empty[s]));
       }
-      if (defer_slot) {  // batch 0 (stage 0) is still staged: its flushed slot now
-        const uint32_t qs = smem_u32(sm.qb[0]);
-        quantize_flushed_group(p, unit, ap.fl_base, ap.fl_gs, qs, ap.fl_slot, smem_u32(sm.f[0]), ct);
-        cwarps_sync();
-        const uint32_t mask = group_mask(p, meta, 0, ap.fl_slot);
-        const int halves = ((mask & 0xffffu) ? 1 : 0) + ((mask >> 16) ? 1 : 0);
-        if (mask && js.take(kCostGroup + kCostGroupHalf * halves) == warp)
-          attend_group<kRec>(st, qrow, lq, qs, ap.fl_slot, mask, p.scale_log2, lane);
-      }
       continue;
     }
-    const int lo = phase == 0 ? 0 : b_begin, hi = phase == 0 ? (has_b0 ? 1 : 0) : b_end;
+    const int lo = phase == 2 ? b_begin : 0;
+    const int hi = phase == 2 ? b_end : (phase == 3 || has_b0 ? 1 : 0);
 #pragma unroll 1
     for (int b = lo; b < hi; ++b) {
       if (!batch_live(p, meta, b)) continue;
-      if (leader) {
-        iss.pump_f(nf);
-        iss.pump_q(meta, nq);
-      }
-      __syncwarp();
-      const uint32_t s = nq % kQStages, ph = (nq / kQStages) & 1;
-      ++nq;
-      if (!aborted && !mbar_wait(smem_u32(&sm.q_full[s]), ph, p.err)) aborted = true;
-      const uint32_t qs = smem_u32(sm.qb[s]);
-      if (ap.sink && b == 0) {  // the sink group changed: re-quantize it into slot 0 (and the cache)
-        p.sink_k16[(unit * p.sink + len - 1) * kHeadDim + ct] = new_kc;  // fp16 copy of the new sink token
-        p.sink_v16[(unit * p.sink + len - 1) * kHeadDim + ct] = new_vc;
-        cwarps_sync();  // the copies are read back by other threads
-        requantize_sink(p, unit, static_cast<int>(len), qs, ct);
-        cwarps_sync();
-      }
-      if (ap.fl_batch == b && !defer_slot) {  // a window group was flushed: quantize it into its slot
-        // (and the cache); the F-tiles were consumed before, and are still staged when resident
-        quantize_flushed_group(p, unit, ap.fl_base, ap.fl_gs, qs, ap.fl_slot, resident ? smem_u32(sm.f[0]) : 0u,
-                               ct);
+      uint32_t qs, s = 0;
+      if (phase != 3) {
+        if (leader) {
+          iss.pump_f(nf);
+          iss.pump_q(meta, nq);
+        }
+        __syncwarp();
+        s = nq % kQStages;
+        const uint32_t ph = (nq / kQStages) & 1;
+        ++nq;
+        if (!aborted && !mbar_wait(smem_u32(&sm.q_full[s]), ph, p.err)) aborted = true;
+        qs = smem_u32(sm.qb[s]);
+        if (appending && ap.sink && b == 0) {  // the sink group changed: re-quantize it into slot 0 (and the cache)
+          p.sink_k16[(unit * p.sink + len - 1) * kHeadDim + ct] = new_kc;  // fp16 copy of the new sink token
+          p.sink_v16[(unit * p.sink + len - 1) * kHeadDim + ct] = new_vc;
+          cwarps_sync();  // the copies are read back by other threads
+          requantize_sink(p, unit, static_cast<int>(len), qs, ct);
+          cwarps_sync();
+        }
+        if (appending && ap.fl_batch == b && !defer_slot) {  // a window group was flushed: quantize it into its
+          // slot (and the cache); the F-tiles were consumed before, and are still staged when resident
+          quantize_flushed_group(p, unit, ap.fl_base, ap.fl_gs, qs, ap.fl_slot, resident ? smem_u32(sm.f[0]) : 0u,
+                                 ct);
+          cwarps_sync();
+        }
+      } else {  // batch 0 (stage 0) is still staged: its flushed slot now
+        qs = smem_u32(sm.qb[0]);
+        quantize_flushed_group(p, unit, ap.fl_base, ap.fl_gs, qs, ap.fl_slot, smem_u32(sm.f[0]), ct);
         cwarps_sync();
       }
 #pragma unroll 1
       for (int gs = 0; gs < kBatchGroups; ++gs) {
+        if (phase == 3 ? gs != ap.fl_slot : (defer_slot && b == 0 && gs == ap.fl_slot)) continue;
         const uint32_t mask = group_mask(p, meta, b, gs);
-        if (!mask || (defer_slot && b == 0 && gs == ap.fl_slot)) continue;
+        if (!mask) continue;
         const int halves = ((mask & 0xffffu) ? 1 : 0) + ((mask >> 16) ? 1 : 0);
         if (js.take(kCostGroup + kCostGroupHalf * halves) != warp) continue;
         attend_group<kRec>(st, qrow, lq, qs, gs, mask, p.scale_log2, lane);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sm.q_empty[s]));
+      if (phase != 3) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sm.q_empty[s]));
+      }
     }
   }
 
@@ -977,11 +993,12 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   }
   if (appending) {
     if (ap.f_item >= 0) {  // the new token's residual slot
-      const int slot = static_cast<int>((len - 1 - p.sink) % p.res_cap);
+      const int slot = (len - 1 - p.sink) % p.res_cap;
       p.k_res[(unit * p.res_cap + slot) * kHeadDim + res_elem(slot, ct)] = new_kc;
       p.v_res[(unit * p.res_cap + slot) * kHeadDim + res_elem(slot, ct)] = new_vc;
     }
-    if (ct == 0) p.unit_lens[unit] = len;  // every thread read the old length at entry
+    if (ct == 0 && len64 >= 0 && len64 < kMaxUnitLen)  // every thread read the old length at entry
+      p.unit_lens[unit] = len;
   }
   __half* out = p.o + unit * kGroupHeads * kHeadDim;
   if (p.ppu == 1) {
@@ -1012,12 +1029,17 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     kivi_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                        const KParams p) {
-  kivi_decode_cta<false>(&tmK, &tmV, p, blockIdx.x);
+  kivi_decode_cta<false, false>(&tmK, &tmV, p, blockIdx.x);
 }
 
-// The streaming cache (every load a 1-D bulk copy).
+// The streaming cache (every load a 1-D bulk copy): attention only, and a
+// decode step (append + attention; its cold paths take p by reference).
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) kivi_stream_decode_kernel(const KParams p) {
-  kivi_decode_cta<true>(nullptr, nullptr, p, blockIdx.x);
+  kivi_decode_cta<true, false>(nullptr, nullptr, p, blockIdx.x);
+}
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
+    kivi_stream_step_kernel(const __grid_constant__ KParams p) {
+  kivi_decode_cta<true, true>(nullptr, nullptr, p, blockIdx.x);
 }
 
 // Several layers (caches of one geometry) in one launch: layer-major CTAs,
@@ -1027,14 +1049,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) kivi_stream_decode_kerne
 constexpr int kMaxLayers = 24;
 struct KiviLayers {
   KParams p[kMaxLayers];
-  int64_t per_layer;
+  unsigned per_layer;
   int n_layers;
 };
 static_assert(sizeof(KiviLayers) <= 32000, "kernel parameter space");
 
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) kivi_decode_layers_kernel(const __grid_constant__ KiviLayers L) {
   const int layer = static_cast<int>(blockIdx.x / L.per_layer);
-  kivi_decode_cta<true>(nullptr, nullptr, L.p[layer], blockIdx.x % L.per_layer);
+  kivi_decode_cta<true, true>(nullptr, nullptr, L.p[layer], static_cast<int>(blockIdx.x % L.per_layer));
 }
 
 struct Plan {
@@ -1055,6 +1077,8 @@ int64_t cta_slots() {
     if (cudaFuncSetAttribute(kivi_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(kivi_stream_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(kivi_stream_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(kivi_decode_layers_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemBytes)) != cudaSuccess ||
@@ -1134,10 +1158,10 @@ int launch(KParams& p, const Plan& s, const void* k_res, const void* v_res, void
   int rc = prepare(p, s, k_res, v_res, ws, wsb, &mk, &mv);
   if (rc) return rc;
   cta_slots();  // sets the shared-memory limit
-  cudaError_t e = p.layout == 0 ? launch_kernel(kivi_decode_kernel, dim3(static_cast<unsigned>(s.grid)),
-                                                dim3(kThreads), kSmemBytes, stream, mk, mv, p)
-                                : launch_kernel(kivi_stream_decode_kernel, dim3(static_cast<unsigned>(s.grid)),
-                                                dim3(kThreads), kSmemBytes, stream, p);
+  const dim3 grid(static_cast<unsigned>(s.grid));
+  cudaError_t e = p.layout == 0 ? launch_kernel(kivi_decode_kernel, grid, dim3(kThreads), kSmemBytes, stream, mk, mv, p)
+                  : p.new_k     ? launch_kernel(kivi_stream_step_kernel, grid, dim3(kThreads), kSmemBytes, stream, p)
+                                : launch_kernel(kivi_stream_decode_kernel, grid, dim3(kThreads), kSmemBytes, stream, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? NSA_OK : cuda_fail(e, "kivi decode launch");
 }
@@ -1204,7 +1228,7 @@ int nsa_kivi_decode(const void* q, const void* k_res, const void* v_res, const v
   p.o = static_cast<__half*>(o);
   p.n_kv_heads = static_cast<int>(n_kv_heads);
   p.layout = 0;
-  p.seq_len = seq_len;
+  p.seq_len = seq_len < kMaxUnitLen ? seq_len : kMaxUnitLen;  // same attended set beyond S + W
   p.window = static_cast<int>(window);
   p.sink = static_cast<int>(sink);
   p.residual = static_cast<int>(residual);
