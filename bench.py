@@ -66,7 +66,7 @@ def algorithmic_bytes(workload: str, batch: int) -> int:
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of ONE launch of the
 # dominant kernel at B=32, from the committed ncu captures of this exact workload.
 NCU_TRAFFIC = {
-    "kivi": (25_653_248, "profiles/kivi_decode_kernel_kivi_W256_L163840_B32.md"),
+    "kivi": (25_626_624, "profiles/kivi_stream_step_kernel_kivi_W256_L163840_B32.md"),
     "sparse": (34_635_008, "profiles/window_decode_kernel_sparse_W256_L163840_B32.md"),
     "dense": (1_078_491_176, "profiles/fp16_decode_kernel_dense_L8192_B32.md"),
 }
@@ -433,8 +433,8 @@ def main():
                      "traffic": (NCU_TRAFFIC[name][0] * B_PER_GPU // 32) if name in NCU_TRAFFIC else None,
                      "traffic_source": (NCU_TRAFFIC[name][1] + " (one ncu capture, cold L2)")
                      if name in NCU_TRAFFIC else None,
-                     "kernel": ("kivi_decode_kernel (quantize-on-append + attention, one launch)"
-                                if wlobj.launches_per_step == 1 else "kivi_decode_kernel (attention)")
+                     "kernel": ("kivi_stream_step_kernel (quantize-on-append + attention, one launch)"
+                                if wlobj.launches_per_step == 1 else "kivi_stream_decode_kernel (attention)")
                      if name == "kivi" else
                      ("window_decode_kernel (one CTA per unit)" if name == "sparse" and
                       B_PER_GPU * HKV >= torch.cuda.get_device_properties(dev).multi_processor_count and
