@@ -248,6 +248,44 @@ int nsa_kivi_stream_decode_step_layers(const nsa_kivi_stream_cache* caches, int6
                                        void* const* o, float sm_scale, void* workspace, size_t workspace_bytes,
                                        nsa_stream_t stream);
 
+/* ------------------------------------------------------------ host buffers
+ * Decode entry points over HOST buffers, for callers whose queries and
+ * outputs live in host memory (the reference's Python functions accept CPU
+ * tensors the caller moves).  A pipe owns `depth` device staging slots (one
+ * input + one output region each) and two copy streams: every call copies
+ * its input in on the pipe's input stream, runs the decode on `stream` and
+ * copies the output back on the pipe's output stream, ordered by events, so
+ * consecutive calls overlap their copies with each other's decode.  A slot
+ * is reused only after its previous decode and output copy have finished.
+ * Host buffers should be pinned for the copies to be asynchronous.
+ * nsa_host_pipe_begin orders the pipe's copies after `stream`'s prior work;
+ * nsa_host_pipe_end orders `stream`'s later work after every output copy
+ * (the outputs are in host memory once that point of `stream` is reached).
+ * A pipe belongs to the device current at its creation.  No reference
+ * counterpart. */
+#define NSA_HOST_PIPE_MAX_DEPTH 8
+typedef struct nsa_host_pipe nsa_host_pipe;
+nsa_host_pipe* nsa_host_pipe_create(size_t in_bytes, size_t out_bytes, int depth); /* NULL on failure */
+void nsa_host_pipe_destroy(nsa_host_pipe* pipe);
+int nsa_host_pipe_begin(nsa_host_pipe* pipe, nsa_stream_t stream);
+int nsa_host_pipe_end(nsa_host_pipe* pipe, nsa_stream_t stream);
+/* nsa_kivi_stream_decode_step with x_host = [q | new_k | new_v] packed
+ * (f16, B*8*Hkv*D + 2*B*Hkv*D elements) and the output to o_host. */
+int nsa_kivi_stream_decode_step_host(nsa_host_pipe* pipe, const nsa_kivi_stream_cache* cache, const void* x_host,
+                                     void* o_host, float sm_scale, void* workspace, size_t workspace_bytes,
+                                     nsa_stream_t stream);
+/* nsa_sparse_decode / nsa_dense_decode with q and o in host memory (the
+ * caches stay on the device). */
+int nsa_sparse_decode_host(nsa_host_pipe* pipe, const void* q_host, const void* k_cache, const void* v_cache,
+                           void* o_host, int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+                           int64_t window, int64_t sink, int64_t seq_len, const int64_t* seq_lens,
+                           const int32_t* ring_heads, float sm_scale, void* workspace, size_t workspace_bytes,
+                           nsa_stream_t stream);
+int nsa_dense_decode_host(nsa_host_pipe* pipe, const void* q_host, const void* k, const void* v, void* o_host,
+                          int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, int64_t cache_len,
+                          int64_t seq_len, float sm_scale, void* workspace, size_t workspace_bytes,
+                          nsa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

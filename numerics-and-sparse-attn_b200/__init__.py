@@ -6,8 +6,10 @@ The kernels live in ``libnsa_b200.so`` (C ABI: include/nsa_b200.h), built by
 ``build.py``; this package is the thin Python host side over it.
 """
 from . import _lib
+from ._lib import HostPipe
 from .constants import *  # noqa: F401,F403
-from .decode import RingCache, dense_decode_attention, sparse_decode_attention
+from .decode import (RingCache, dense_decode_attention, dense_decode_attention_host, sparse_decode_attention,
+                     sparse_decode_attention_host)
 from .kivi import (KiviCache, build_quantized_kv_cache, decode_step_layers, dequantize_k, dequantize_v,
                    quantize_k_cache, quantize_v_cache, sparse_decode_attention_quantized)
 
@@ -23,6 +25,9 @@ __all__ = [
     "KiviCache",
     "decode_step_layers",
     "RingCache",
+    "HostPipe",
+    "dense_decode_attention_host",
+    "sparse_decode_attention_host",
     "native_library_path",
     "device_error",
 ]

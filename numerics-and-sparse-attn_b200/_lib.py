@@ -58,6 +58,13 @@ PROTOTYPES = {
     "nsa_ring_append": (_INT, [_P, _P, _P, _P, _P] + [_I64] * 5 + [_P]),
     "nsa_ring_decode": (_INT, [_P, _P, _P, _P] + [_I64] * 6 + [_P, _F, _P, _SZ, _P]),
     "nsa_ring_decode_step": (_INT, [_P, _P, _P, _P] + [_I64] * 6 + [_P, _P, _P, _F, _P, _SZ, _P]),
+    "nsa_host_pipe_create": (_P, [_SZ, _SZ, _INT]),
+    "nsa_host_pipe_destroy": (None, [_P]),
+    "nsa_host_pipe_begin": (_INT, [_P, _P]),
+    "nsa_host_pipe_end": (_INT, [_P, _P]),
+    "nsa_kivi_stream_decode_step_host": (_INT, [_P, _P, _P, _P, _F, _P, _SZ, _P]),
+    "nsa_sparse_decode_host": (_INT, [_P, _P, _P, _P, _P] + [_I64] * 7 + [_P, _P, _F, _P, _SZ, _P]),
+    "nsa_dense_decode_host": (_INT, [_P, _P, _P, _P, _P] + [_I64] * 6 + [_F, _P, _SZ, _P]),
 }
 
 _lock = threading.Lock()
@@ -135,3 +142,43 @@ def workspace(device: torch.device, nbytes: int, stream: int | None = None) -> t
             ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
             _workspaces[key] = ws
     return ws
+
+
+class HostPipe:
+    """Device staging slots and copy streams for the host-buffer entry points
+    (nsa_host_pipe in include/nsa_b200.h): ``depth`` slots of ``in_bytes`` of
+    input and ``out_bytes`` of output on ``device``.  Consecutive host-buffer
+    calls through one pipe overlap their copies with each other's decode;
+    ``begin()`` / ``end()`` order the pipe's copies after / before the current
+    stream's work (the outputs are in host memory once the stream passes
+    ``end()``)."""
+
+    def __init__(self, in_bytes: int, out_bytes: int, device=None, depth: int = 2):
+        dev = torch.device(device) if device is not None else torch.device("cuda")
+        self.device = dev if dev.index is not None else torch.device("cuda", torch.cuda.current_device())
+        self.in_bytes, self.out_bytes, self.depth = int(in_bytes), int(out_bytes), int(depth)
+        lib = load()
+        with on_device(self.device):
+            h = lib.nsa_host_pipe_create(self.in_bytes, self.out_bytes, self.depth)
+        if not h:
+            raise NativeError("nsa_host_pipe_create: " + lib.nsa_last_error_message().decode(errors="replace"))
+        self.handle = h
+
+    def begin(self, stream: int | None = None) -> None:
+        with on_device(self.device):
+            check(load().nsa_host_pipe_begin(self.handle, stream_handle(self.device) if stream is None else stream))
+
+    def end(self, stream: int | None = None) -> None:
+        with on_device(self.device):
+            check(load().nsa_host_pipe_end(self.handle, stream_handle(self.device) if stream is None else stream))
+
+    def close(self) -> None:
+        h, self.handle = getattr(self, "handle", None), None
+        if h:
+            load().nsa_host_pipe_destroy(h)
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown
+            pass

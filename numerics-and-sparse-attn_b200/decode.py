@@ -68,6 +68,67 @@ def dense_decode_attention(q, k, v, seq_len, sm_scale=None):
     return o
 
 
+def _check_host(name, t, shape):
+    _require(isinstance(t, torch.Tensor) and not t.is_cuda and t.dtype == torch.float16 and t.is_contiguous()
+             and tuple(t.shape) == tuple(shape),
+             f"{name} must be a contiguous float16 host tensor of shape {tuple(shape)} (pinned for overlap)")
+
+
+def dense_decode_attention_host(pipe, q_host, o_host, k, v, seq_len, sm_scale=None):
+    """dense_decode_attention with the query and the output in host memory
+    (``pipe``: a _lib.HostPipe on k's device): copy in, decode and copy out
+    are queued on the pipe's streams and the current stream; o_host holds the
+    result once the stream passes ``pipe.end()``."""
+    _check_fp16_cuda("k", k, 4)
+    _check_fp16_cuda("v", v, 4)
+    b, hkv, cache_len, d = k.shape
+    _require(k.shape == v.shape and d == D_HEAD and v.device == k.device, "k and v must match, head_dim 128")
+    _check_host("q_host", q_host, (b, 8 * hkv, d))
+    _check_host("o_host", o_host, (b, 8 * hkv, d))
+    seq_len = int(seq_len)
+    lib = _lib.load()
+    with _lib.on_device(k.device):
+        stream = _lib.stream_handle(k.device)
+        ws = _lib.workspace(k.device, lib.nsa_dense_workspace_bytes(b, hkv, seq_len), stream)
+        _lib.check(lib.nsa_dense_decode_host(pipe.handle, q_host.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                             o_host.data_ptr(), b, 8 * hkv, hkv, d, cache_len, seq_len,
+                                             float(D_HEAD ** -0.5 if sm_scale is None else sm_scale),
+                                             ws.data_ptr(), ws.numel(), stream))
+
+
+def sparse_decode_attention_host(pipe, q_host, o_host, k_cache, v_cache, seq_len, window, sink=SINK_SIZE,
+                                 sm_scale=None, *, ring_head=None, seq_lens=None):
+    """sparse_decode_attention with the query and the output in host memory
+    (``pipe``: a _lib.HostPipe on the cache's device); ring_head / seq_lens as
+    there (device tensors).  o_host holds the result once the stream passes
+    ``pipe.end()``."""
+    _check_fp16_cuda("k_cache", k_cache, 4)
+    _check_fp16_cuda("v_cache", v_cache, 4)
+    b, hkv, slots, d = k_cache.shape
+    window, sink, seq_len = int(window), int(sink), int(seq_len)
+    _require(k_cache.shape == v_cache.shape and d == D_HEAD and slots == sink + window,
+             "k_cache / v_cache must be [B, Hkv, sink+window, 128] and match")
+    _check_host("q_host", q_host, (b, 8 * hkv, d))
+    _check_host("o_host", o_host, (b, 8 * hkv, d))
+    heads_ptr = lens_ptr = None
+    if ring_head is not None:
+        _require(isinstance(ring_head, torch.Tensor) and ring_head.dtype == torch.int32 and ring_head.is_cuda
+                 and ring_head.numel() == b, "ring_head must be an int32 CUDA tensor of length B")
+        heads_ptr = ring_head.data_ptr()
+    if seq_lens is not None:
+        _require(isinstance(seq_lens, torch.Tensor) and seq_lens.dtype == torch.int64 and seq_lens.is_cuda
+                 and seq_lens.numel() == b, "seq_lens must be an int64 CUDA tensor of length B")
+        lens_ptr = seq_lens.data_ptr()
+    lib = _lib.load()
+    with _lib.on_device(k_cache.device):
+        stream = _lib.stream_handle(k_cache.device)
+        ws = _lib.workspace(k_cache.device, lib.nsa_sparse_workspace_bytes(b, hkv, window, sink), stream)
+        _lib.check(lib.nsa_sparse_decode_host(pipe.handle, q_host.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                              o_host.data_ptr(), b, 8 * hkv, hkv, d, window, sink, seq_len, lens_ptr,
+                                              heads_ptr, float(D_HEAD ** -0.5 if sm_scale is None else sm_scale),
+                                              ws.data_ptr(), ws.numel(), stream))
+
+
 def sparse_decode_attention(q, k_cache, v_cache, seq_len, window, sink=SINK_SIZE, sm_scale=None, *,
                             ring_head=None, seq_lens=None):
     """StreamingLLM sink + sliding-window decode (sparse_kernel.py:105-118).

@@ -388,6 +388,24 @@ class KiviCache:
                 float(sm_scale), ws.data_ptr(), ws.numel(), stream))
         return out
 
+    def decode_step_host(self, pipe, x_host, o_host, sm_scale=None):
+        """decode_step with its inputs and output in host memory: x_host =
+        [q | new_k | new_v] packed (float16, B*8*Hkv*D + 2*B*Hkv*D elements),
+        o_host like q.  ``pipe``: a _lib.HostPipe on the cache's device; the
+        copies overlap other calls' decode, and o_host holds the result once
+        the stream passes ``pipe.end()``."""
+        n_q = self.batch * 8 * self.n_kv_heads * self.head_dim
+        n_x = n_q + 2 * self.batch * self.n_kv_heads * self.head_dim
+        for name, t, n in (("x_host", x_host, n_x), ("o_host", o_host, n_q)):
+            _req(isinstance(t, torch.Tensor) and not t.is_cuda and t.dtype == torch.float16 and t.is_contiguous()
+                 and t.numel() == n, f"{name} must be a contiguous float16 host tensor of {n} elements")
+        with _lib.on_device(self.device):
+            stream = _lib.stream_handle(self.device)
+            ws = _lib.workspace(self.device, self._ws_bytes, stream)
+            _lib.check(_lib.load().nsa_kivi_stream_decode_step_host(
+                pipe.handle, ctypes.byref(self._desc), x_host.data_ptr(), o_host.data_ptr(),
+                float(self.head_dim ** -0.5 if sm_scale is None else sm_scale), ws.data_ptr(), ws.numel(), stream))
+
     # ---------------------------------------------------------------- filling
     def load_state(self, seq_len, sink_k, sink_v, tail_k=None, tail_v=None, tail_start=None):
         """Set the cache to its state after ``seq_len`` appends.
