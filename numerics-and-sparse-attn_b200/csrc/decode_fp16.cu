@@ -450,9 +450,9 @@ __global__ void __launch_bounds__(win::kThreads, 2)
       if (any0 && any1) {
         st.consume_rows<2>(sd, sd + win::kTile, win::kRegion, r, vl, vh, p.scale_log2, lane);
       } else {
-        const int h = any0 ? 0 : 1;
-        const bool l1[1] = {vl[h]}, h1[1] = {vh[h]};
-        st.consume_rows<1>(sd, sd + win::kTile, win::kRegion, r + 16 * h, l1, h1, p.scale_log2, lane);
+        // (selects, not vl[h]: a dynamic index would put the flags in local memory)
+        const bool l1[1] = {any0 ? vl[0] : vl[1]}, h1[1] = {any0 ? vh[0] : vh[1]};
+        st.consume_rows<1>(sd, sd + win::kTile, win::kRegion, r + (any0 ? 0 : 16), l1, h1, p.scale_log2, lane);
       }
     }
     __syncwarp();
