@@ -13,14 +13,30 @@ REF_COLS_Q = ["L", "W", "ms_dense", "ms_sparse", "ms_quantized", "bytes_sparse_p
 
 def test_sweep_columns_and_byte_model(tmp_path):
     timer = benchmark.Timer(reps=2, warmup=1)
-    rows = benchmark.benchmark([8192], [0, 256], timer, 6.45)
+    rows = benchmark.benchmark([8192], [0, 256], timer, 6.45, 32)
     assert [r["W"] for r in rows] == [0, 256]
     assert list(rows[0])[:len(REF_COLS)] == REF_COLS
     assert all(r["ms_sparse"] > 0 and r["ms_dense"] > 0 for r in rows)
     assert rows[1]["predicted_ratio"] == pytest.approx((1_048_576 + 131_072 * 8192) / (1_048_576 + 131_072 * 260))
-    rows_q = benchmark.benchmark_quantized([8192], [0, 256], timer, 6.45)
+    rows_q = benchmark.benchmark_quantized([8192], [0, 256], timer, 6.45, 32)
     assert [r["W"] for r in rows_q] == [256]  # W < 128 is skipped, as in the reference
     assert list(rows_q[0])[:len(REF_COLS_Q)] == REF_COLS_Q
     assert rows_q[0]["bytes_quantized_pred"] == 21_757_952  # the csv's own W=256 figure
     benchmark.save(rows_q, str(tmp_path / "q.csv"))
     assert (tmp_path / "q.csv").read_text().splitlines()[0].startswith(",".join(REF_COLS_Q))
+
+
+def test_graph_columns_and_batch_scaling():
+    """--graph adds back-to-back CUDA-graph timings over L2-exceeding cache
+    rotations; a batch other than 32 scales the byte model with it."""
+    timer = benchmark.Timer(reps=2, warmup=1)
+    g = benchmark.GraphTimer(reps=4, per_graph=8)
+    rows = benchmark.benchmark([8192], [256], timer, 6.45, 64, g)
+    r = rows[0]
+    assert r["batch"] == 64 and r["n_gpus"] == 1
+    assert r["ms_sparse_graph"] > 0 and r["ms_dense_graph"] > 0
+    assert r["tbs_sparse_graph"] == pytest.approx(2 * (1_048_576 + 131_072 * 260) / r["ms_sparse_graph"] / 1e9)
+    rows_q = benchmark.benchmark_quantized([8192], [256], timer, 6.45, 64, g)
+    assert rows_q[0]["bytes_quantized_pred"] == 2 * 21_757_952
+    assert rows_q[0]["ms_quantized_graph"] > 0
+    assert benchmark.n_copies(35_127_296) * 35_127_296 > 2 * benchmark.L2_BYTES
