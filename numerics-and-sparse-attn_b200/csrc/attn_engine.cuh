@@ -276,10 +276,11 @@ __device__ __forceinline__ void warp_publish(const WarpAttn& st, EpilogueSmem& e
   }
 }
 
-// Merge the published group-0 warp states for one head and 4 consecutive dims.
+// Merge the published group-0 warp states for one head and N consecutive dims.
 // Returns the normalized output in o[4] and the piece's log2-sum-exp in lse
 // (-inf when the piece saw no valid token; o is then 0/0 = NaN).
-__device__ __forceinline__ void merge_warps(const EpilogueSmem& ep, int head, int d0, float (&o)[4], float& lse) {
+template <int N>
+__device__ __forceinline__ void merge_warps(const EpilogueSmem& ep, int head, int d0, float (&o)[N], float& lse) {
   float mstar = -INFINITY;
 #pragma unroll
   for (int w = 0; w < kGroupWarps; ++w) mstar = fmaxf(mstar, ep.red.m[w][head]);
@@ -292,7 +293,7 @@ __device__ __forceinline__ void merge_warps(const EpilogueSmem& ep, int head, in
     L += f[w] * ep.red.l[w][head];
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < N; ++i) {
     float a = 0.f;
 #pragma unroll
     for (int w = 0; w < kGroupWarps; ++w) a += f[w] * ep.red.o[w][head][d0 + i];
@@ -306,6 +307,14 @@ __device__ __forceinline__ void store_half4(__half* dst, const float (&o)[4]) {
   v.x = pack_half2(o[0], o[1]);
   v.y = pack_half2(o[2], o[3]);
   *reinterpret_cast<uint2*>(dst) = v;
+}
+__device__ __forceinline__ void store_half8(__half* dst, const float (&o)[8]) {  // dst 16-byte aligned
+  uint4 v;
+  v.x = pack_half2(o[0], o[1]);
+  v.y = pack_half2(o[2], o[3]);
+  v.z = pack_half2(o[4], o[5]);
+  v.w = pack_half2(o[6], o[7]);
+  *reinterpret_cast<uint4*>(dst) = v;
 }
 
 // Split-K partials of one unit: `n` pieces, each [8 heads] lse and

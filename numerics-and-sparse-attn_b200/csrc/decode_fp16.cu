@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ct = threadIdx.x;  // 0..255
     const int hh = ct >> 5, d0 = (ct & 31) * 4;
     float o[4], lse;
-    merge_warps(sm.ep, hh, d0, o, lse);
+    merge_warps<4>(sm.ep, hh, d0, o, lse);
     __half* out = p.o + pc.unit * kGroupHeads * kHeadDim;
     if (pc.n_pieces == 1) {
       store_half4(out + hh * kHeadDim + d0, o);
@@ -347,7 +347,11 @@ __global__ void __launch_bounds__(win::kThreads, 2)
                          const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   grid_launch_dependents();
-  grid_dependency_wait();  // the cache and q may come from the previous kernel of the stream
+  // the cache and q may come from the previous kernel of the stream: global
+  // memory is touched only after this wait (attention alone first initialises
+  // its barriers, which measured faster)
+  const bool appending = p.new_k != nullptr;
+  if (appending) grid_dependency_wait();
   if (smem_u32(smem_raw) & 1023u) {  // TMA tile destinations need 1024-byte alignment
     if (threadIdx.x == 0) set_error(p.err, NSA_ERR_ALIGN);
     return;
@@ -364,6 +368,7 @@ __global__ void __launch_bounds__(win::kThreads, 2)
     fence_barrier_init();
   }
   __syncthreads();
+  if (!appending) grid_dependency_wait();
 
   // Tile i uses stage i % kStages; it is issued once warp 0 itself has
   // consumed tile i - kStages (the other warps' release is then waited for).
@@ -389,7 +394,6 @@ __global__ void __launch_bounds__(win::kThreads, 2)
   // one-launch append: position pos = the unit's old length goes to slot
   // `aslot` (tile aslot / kRows); the staged tile's row is patched by the warp
   // whose job holds it, the cache slot and the length are stored at the end
-  const bool appending = p.new_k != nullptr;
   int64_t pos = 0;
   int aslot = -1;
   if (appending) {
@@ -464,12 +468,9 @@ __global__ void __launch_bounds__(win::kThreads, 2)
   warp_publish(st, sm.ep, warp, lane);
   win::sync4();
   const int hh = ct >> 4, d0 = (ct & 15) * 8;  // this thread's head and 8 dims
-  float o4[4], lse;
-  __half* out = p.o + unit * kGroupHeads * kHeadDim + hh * kHeadDim + d0;
-  merge_warps(sm.ep, hh, d0, o4, lse);
-  store_half4(out, o4);
-  merge_warps(sm.ep, hh, d0 + 4, o4, lse);
-  store_half4(out + 4, o4);
+  float o8[8], lse;
+  merge_warps<8>(sm.ep, hh, d0, o8, lse);
+  store_half8(p.o + unit * kGroupHeads * kHeadDim + hh * kHeadDim + d0, o8);
   if (appending) {  // every thread read the old length at entry
     const int64_t cap = p.sink + p.window;
     if (aslot >= 0) {

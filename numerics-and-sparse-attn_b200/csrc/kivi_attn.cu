@@ -776,7 +776,11 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
                                                 int bid) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   grid_launch_dependents();
-  grid_dependency_wait();  // the cache and q may come from the previous kernel of the stream
+  // the cache and q may come from the previous kernel of the stream: global
+  // memory is touched only after this wait (an attention-only launch first
+  // initialises its barriers, which measured faster; a step launch measured
+  // faster waiting first)
+  if constexpr (kAppend) grid_dependency_wait();
   if (smem_u32(smem_raw) & 1023u) {  // TMA tile destinations need 1024-byte alignment
     if (threadIdx.x == 0) set_error(p.err, NSA_ERR_ALIGN);
     return;
@@ -804,6 +808,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
     fence_barrier_init();
   }
   __syncthreads();
+  if constexpr (!kAppend) grid_dependency_wait();
 
   // ------------------------------------------------------------- prologue
   // Global loads of every thread go out first (the query -- 16 bytes per
@@ -984,13 +989,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   cwarps_sync();
   const int hh = ct >> 4, d0 = (ct & 15) * 8;  // this thread's head and 8 dims
   float o[8], lse;
-  {
-    float o4[4];
-    merge_warps(sm.ep, hh, d0, o4, lse);
-    for (int i = 0; i < 4; ++i) o[i] = o4[i];
-    merge_warps(sm.ep, hh, d0 + 4, o4, lse);
-    for (int i = 0; i < 4; ++i) o[4 + i] = o4[i];
-  }
+  merge_warps<8>(sm.ep, hh, d0, o, lse);
   if (appending) {
     if (ap.f_item >= 0) {  // the new token's residual slot
       const int slot = (len - 1 - p.sink) % p.res_cap;
@@ -1002,9 +1001,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   }
   __half* out = p.o + unit * kGroupHeads * kHeadDim;
   if (p.ppu == 1) {
-    const float a[4] = {o[0], o[1], o[2], o[3]}, b[4] = {o[4], o[5], o[6], o[7]};
-    store_half4(out + hh * kHeadDim + d0, a);
-    store_half4(out + hh * kHeadDim + d0 + 4, b);
+    store_half8(out + hh * kHeadDim + d0, o);
     return;
   }
   const int64_t pidx = unit * p.ppu + piece;
