@@ -237,7 +237,30 @@ def cpu_baseline(name: str, budget_s: float = 10.0):
 
 
 # ----------------------------------------------------------------- main
+_STDOUT_FD = None
+
+
+def quiet_stdout():
+    """Send everything written to file descriptor 1 (NCCL's and other
+    libraries' banners included) to stderr, so that stdout carries only the
+    JSON line emit() prints."""
+    global _STDOUT_FD
+    if _STDOUT_FD is None:
+        sys.stdout.flush()
+        _STDOUT_FD = os.dup(1)
+        os.dup2(2, 1)
+
+
+def emit(obj) -> None:
+    """Print the one JSON line on the real stdout."""
+    sys.stdout.flush()
+    if _STDOUT_FD is not None:
+        os.dup2(_STDOUT_FD, 1)
+    print(json.dumps(obj), flush=True)
+
+
 def main():
+    quiet_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
@@ -270,14 +293,13 @@ def main():
                 break
         sec = statistics.mean(steps)
         v = B_PER_GPU / sec
-        print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
-                          "steps": len(steps), "warmup": a.warmup, "ms_per_step": sec * 1e3,
-                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-                          "data": "synthetic N(0,1), seeded", "config": config,
-                          "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-                                           "sample": f"{len(steps)} steps of B={B_PER_GPU} on {threads} threads"},
-                          "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                                  "d2h_bytes_per_step": 0}}))
+        emit({"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
+              "steps": len(steps), "warmup": a.warmup, "ms_per_step": sec * 1e3,
+              "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+              "data": "synthetic N(0,1), seeded", "config": config,
+              "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                               "sample": f"{len(steps)} steps of B={B_PER_GPU} on {threads} threads"},
+              "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
         return
 
     torch.cuda.set_device(local)
@@ -498,7 +520,7 @@ def main():
         del g_step, g_attn
         torch.distributed.destroy_process_group()
     if rank == 0:
-        print(json.dumps(line))
+        emit(line)
 
 
 if __name__ == "__main__":
