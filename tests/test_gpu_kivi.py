@@ -291,6 +291,38 @@ def test_fused_step_equals_append_then_attend(W):
                 np.testing.assert_array_equal(a[key], b[key], err_msg=f"{key} at L={L}")
 
 
+def test_fused_step_multi_batch_window():
+    """W=1024 (28 window groups: six Q-batches refilled through the two-stage
+    ring while the warps work): fused decode steps across a group flush match
+    the oracle, give append + attend's outputs (bit for bit off flush steps)
+    and leave the same cache state."""
+    B, Hkv, W, L, S, R = 32, 8, 1024, 163_840, 4, 128
+    fused = quant_kernel.KiviCache.synthetic(B, Hkv, W, L, device=DEV,
+                                             generator=torch.Generator(device=DEV).manual_seed(9))
+    split = quant_kernel.KiviCache.synthetic(B, Hkv, W, L, device=DEV,
+                                             generator=torch.Generator(device=DEV).manual_seed(9))
+    assert fused.step_launches() == 1
+    geom = ok.StreamGeometry(window=W)
+    g = torch.Generator(device=DEV).manual_seed(10)
+    for step in range(36):
+        q = torch.randn(B, 64, 128, device=DEV, generator=g).half()
+        nk = torch.randn(B, Hkv, 128, device=DEV, generator=g).half()
+        nv = torch.randn(B, Hkv, 128, device=DEV, generator=g).half()
+        o_f = fused.decode_step(q, nk, nv)
+        split.append(nk, nv)
+        o_s = split.attend(q)
+        if (L + step - S + 1 - R) % 32 == 0:  # this append flushes a group
+            assert _err(o_f, o_s) < 2e-3, step
+        else:
+            assert torch.equal(o_f, o_s), step
+        if step in (0, 27, 28, 35):
+            ref = oa.stream_attention(q, _state_np(fused), L + step + 1, geom)
+            assert _err(o_f, ref) < TOL_2BIT, step
+    a, b = _state_np(fused), _state_np(split)
+    for key in a:
+        np.testing.assert_array_equal(a[key], b[key], err_msg=key)
+
+
 def test_layer_batched_step_equals_per_layer_steps():
     """decode_step_layers (3 layers in one launch) gives the same outputs and
     cache states, bit for bit, as KiviCache.decode_step layer by layer, over
