@@ -52,6 +52,10 @@ const char* nsa_last_error_message(void);
 /* Synchronize `stream`, then read and clear the device error word of the
  * current device into *code (NSA_OK if no kernel recorded an error). */
 int nsa_device_error(int* code, nsa_stream_t stream);
+/* Self-test of the failure path: one CTA waits, limit_ns at most, on a
+ * barrier phase that nothing completes; the wait gives up and records
+ * NSA_ERR_TIMEOUT for nsa_device_error, and the context stays usable. */
+int nsa_selftest_wait_timeout(int64_t limit_ns, nsa_stream_t stream);
 /* Library version string. */
 const char* nsa_version(void);
 

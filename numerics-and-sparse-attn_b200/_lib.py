@@ -37,6 +37,7 @@ PROTOTYPES = {
     "nsa_error_string": (ctypes.c_char_p, [_INT]),
     "nsa_last_error_message": (ctypes.c_char_p, []),
     "nsa_device_error": (_INT, [ctypes.POINTER(_INT), _P]),
+    "nsa_selftest_wait_timeout": (_INT, [_I64, _P]),
     "nsa_version": (ctypes.c_char_p, []),
     "nsa_dense_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
     "nsa_dense_decode": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _F, _P, _SZ, _P]),

@@ -4,6 +4,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "common.cuh"
 #include "host_util.h"
 
 namespace nsa {
@@ -153,3 +154,33 @@ int nsa_device_error(int* code, nsa_stream_t stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- self-test
+// One CTA waits, with a limit of limit_ns, on an mbarrier phase that nothing
+// completes: the bounded wait gives up, records NSA_ERR_TIMEOUT in the
+// device error word and the kernel returns -- the path every kernel takes
+// when a copy never lands.  The context stays usable.
+namespace nsa {
+namespace {
+__global__ void wait_timeout_kernel(int* err, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  const uint32_t b = smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    mbar_init(b, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(b, 0, err, limit_ns);  // phase 0 never completes
+}
+}  // namespace
+}  // namespace nsa
+
+extern "C" int nsa_selftest_wait_timeout(int64_t limit_ns, nsa_stream_t stream) {
+  nsa::clear_error();
+  if (limit_ns <= 0 || limit_ns > 2000000000ll) return nsa::fail(NSA_ERR_INVALID, "limit_ns must be in (0, 2e9]");
+  int* w = nsa::device_error_word();
+  if (!w) return nsa::fail(NSA_ERR_CUDA, "device error word unavailable");
+  nsa::wait_timeout_kernel<<<1, 32, 0, stream>>>(w, static_cast<uint64_t>(limit_ns));
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? NSA_OK : nsa::cuda_fail(e, "wait_timeout_kernel launch");
+}

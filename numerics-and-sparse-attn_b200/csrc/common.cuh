@@ -75,13 +75,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait: returns false (and records NSA_ERR_TIMEOUT) if the phase has
-// not completed within kWaitTimeoutNs.  Callers then leave the kernel.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
+// not completed within limit_ns (default kWaitTimeoutNs).  Callers then leave
+// the kernel.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err,
+                                          uint64_t limit_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 15u) == 0 && globaltimer() - t0 > kWaitTimeoutNs) {
+    if ((i & 15u) == 0 && globaltimer() - t0 > limit_ns) {
       set_error(err, NSA_ERR_TIMEOUT);
       return false;
     }
