@@ -243,7 +243,7 @@ int nsa_kivi_stream_decode_step(const nsa_kivi_stream_cache* cache, const void* 
 /* nsa_kivi_stream_decode_step for n_layers caches of one geometry (caches:
  * host array of n_layers descriptors; new_k, new_v, q, o: host arrays of
  * n_layers device pointers), results as n_layers separate calls.  When the
- * step runs in one launch per layer, up to 24 layers share one launch
+ * step runs in one launch per layer, up to 64 layers share one launch
  * (layer-major CTAs): the launch's fixed costs are paid once.  For decode
  * loops that have every layer's query at once.  The workspace is the
  * single-layer one.  No reference counterpart. */

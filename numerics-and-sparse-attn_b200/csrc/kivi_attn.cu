@@ -1043,7 +1043,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 // `per_layer` of them per layer.  Amortises the launch's fixed costs (start,
 // first-byte latency, tail) over all layers when the decode loop has every
 // layer's query at once.
-constexpr int kMaxLayers = 24;
+constexpr int kMaxLayers = 64;
 struct KiviLayers {
   KParams p[kMaxLayers];
   unsigned per_layer;

@@ -233,7 +233,7 @@ def _res_perm(n_slots, device):
 
 def decode_step_layers(caches, qs, new_ks, new_vs, sm_scale=None):
     """KiviCache.decode_step for several layers' caches (one geometry) at once:
-    returns the list of outputs.  Up to 24 layers share one kernel launch
+    returns the list of outputs.  Up to 64 layers share one kernel launch
     (nsa_kivi_stream_decode_step_layers) when the step fits one launch per layer."""
     n = len(caches)
     _req(len(qs) == n and len(new_ks) == n and len(new_vs) == n, "one q, new_k and new_v per cache")
