@@ -118,6 +118,7 @@ struct Smem {
   __half newtok[2][kHeadDim];             // appended token's K and V (fused append)
   uint64_t f_full[kFStages], f_empty[kFStages];
   uint64_t q_full[kQStages], q_empty[kQStages];
+  int q_rel[kQStages];  // warps that have released the stage's current Q-batch
 };
 
 static_assert(offsetof(Smem, f) == 0 && kFStageBytes % 1024 == 0 && kFRegion % 1024 == 0, "TMA tile destinations");
@@ -240,6 +241,8 @@ __device__ __forceinline__ bool res_slot_valid(const KParams& p, const KiviMeta&
 // its sink group is loaded before the unit's length is known.
 __device__ __forceinline__ bool batch_live(const KParams& p, const KiviMeta& m, int b) {
   if (b == 0) return true;
+  // a full ring whose oldest group still holds an attended token: every slot is live
+  if (m.n_grp == p.n_groups && m.tok_skip < 32) return kBatchGroups * b <= p.n_groups;
   for (int s = 0; s < kBatchGroups; ++s)
     if (group_mask(p, m, b, s)) return true;
   return false;
@@ -804,6 +807,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
     for (int s = 0; s < kQStages; ++s) {
       mbar_init(smem_u32(&sm.q_full[s]), 1);
       mbar_init(smem_u32(&sm.q_empty[s]), kCWarps);
+      sm.q_rel[s] = 0;
     }
     fence_barrier_init();
   }
@@ -883,10 +887,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
     if (phase == 1) {
 #pragma unroll 1
       for (int f = f_begin; f < f_end; ++f) {
-        if (leader) {
-          iss.pump_f(nf);
-          iss.pump_q(meta, nq);
-        }
+        if (leader) iss.pump_f(nf);
         __syncwarp();
         const uint32_t s = nf % kFStages, ph = (nf / kFStages) & 1;
         ++nf;
@@ -939,10 +940,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
       if (!batch_live(p, meta, b)) continue;
       uint32_t qs, s = 0;
       if (phase != 3) {
-        if (leader) {
-          iss.pump_f(nf);
-          iss.pump_q(meta, nq);
-        }
+        if (leader) iss.pump_f(nf);
         __syncwarp();
         s = nq % kQStages;
         const uint32_t ph = (nq / kQStages) & 1;
@@ -976,9 +974,27 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
         if (js.take(kCostGroup + kCostGroupHalf * halves) != warp) continue;
         attend_group<kRec>(st, qrow, lq, qs, gs, mask, p.scale_log2, lane);
       }
-      if (phase != 3) {
+      if (phase != 3) {  // release the stage; the last warp to do so refills it
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&sm.q_empty[s]));
+        if (lane == 0) {
+          __threadfence_block();  // this warp's reads of the stage come first
+          if (atomicAdd(&sm.q_rel[s], 1) == kCWarps - 1) {
+            sm.q_rel[s] = 0;
+            __threadfence_block();
+            // the stage's next batch is two live batches on in the issue order
+            // (batch 0, then the live batches from b_begin)
+            const auto succ = [&](int x) {
+              int y = x == 0 ? b_begin : x + 1;
+              while (y < b_end && !batch_live(p, meta, y)) ++y;
+              return y;
+            };
+            const int b1 = succ(b), b2 = b1 < b_end ? succ(b1) : b_end;
+            if (b2 < b_end) {
+              fence_proxy_async_smem();
+              iss.batch(b2, s);
+            }
+          }
+        }
       }
     }
   }
