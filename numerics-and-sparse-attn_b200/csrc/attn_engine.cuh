@@ -205,9 +205,9 @@ struct WarpAttn {
 };
 
 // Cross-warp merge buffers for the epilogue of one (unit, token-range) piece.
-// Round 1: each warp of group 1 hands its raw state to the warp of group 0
+// First, each warp of group 1 hands its raw state to the warp of group 0
 // with the same index (identical fragment layout, so the merge is
-// element-wise in registers).  Round 2: the group-0 warps publish their
+// element-wise in registers).  Then the group-0 warps publish their
 // merged states to `red`, which aliases `xfer`.  red.o rows are padded to
 // 132 floats so the fragment scatter is conflict-free.
 constexpr int kRedStride = 132;

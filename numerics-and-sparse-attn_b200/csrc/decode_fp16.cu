@@ -348,10 +348,9 @@ __global__ void __launch_bounds__(win::kThreads, 2)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   grid_launch_dependents();
   // the cache and q may come from the previous kernel of the stream: global
-  // memory is touched only after this wait (attention alone first initialises
-  // its barriers, which measured faster)
+  // memory is touched only after the wait below (the barriers are initialised
+  // first, which measured faster for attention alone and for append + attend)
   const bool appending = p.new_k != nullptr;
-  if (appending) grid_dependency_wait();
   if (smem_u32(smem_raw) & 1023u) {  // TMA tile destinations need 1024-byte alignment
     if (threadIdx.x == 0) set_error(p.err, NSA_ERR_ALIGN);
     return;
@@ -368,7 +367,7 @@ __global__ void __launch_bounds__(win::kThreads, 2)
     fence_barrier_init();
   }
   __syncthreads();
-  if (!appending) grid_dependency_wait();
+  grid_dependency_wait();
 
   // Tile i uses stage i % kStages; it is issued once warp 0 itself has
   // consumed tile i - kStages (the other warps' release is then waited for).
