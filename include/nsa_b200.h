@@ -14,7 +14,9 @@
  *   q, o       [B, H, D]          H = 8 * Hkv (GQA group 8), D = 128
  *   k, v       [B, Hkv, L, D]
  * Grids are derived from the shapes passed in (the reference sized them from
- * module constants), so any batch size and any Hkv are accepted.
+ * module constants), so any batch size and any Hkv are accepted.  An empty
+ * batch (B = 0) launches nothing and returns NSA_OK; its tensor pointers may
+ * then be NULL (what zero-size tensors carry).
  *
  * Errors: argument problems are reported synchronously (NSA_ERR_INVALID,
  * NSA_ERR_ALIGN, NSA_ERR_UNSUPPORTED, NSA_ERR_WORKSPACE) with a message from

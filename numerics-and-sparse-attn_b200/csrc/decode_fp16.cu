@@ -553,6 +553,12 @@ Split plan(int64_t n_units, int64_t range_slots) {
   s.n_units = n_units;
   s.tiles_per_unit = range_slots > 0 ? (range_slots + kTile - 1) / kTile : 1;
   s.total_tiles = n_units * s.tiles_per_unit;
+  if (s.total_tiles == 0) {  // empty batch: nothing to split (and nothing is launched)
+    s.n_ctas = 1;
+    s.max_pieces = 1;
+    s.unit_aligned = 1;
+    return s;
+  }
   const int sms = current_device().sm_count > 0 ? current_device().sm_count : 148;
   s.n_ctas = static_cast<int>(s.total_tiles < sms ? s.total_tiles : sms);
   if (s.n_ctas < 1) s.n_ctas = 1;
@@ -585,8 +591,9 @@ size_t workspace_bytes(const Split& s) {
 
 int check_common(const void* q, const void* k, const void* v, const void* o, int64_t batch, int64_t n_heads,
                  int64_t n_kv_heads, int64_t head_dim) {
-  if (!q || !k || !v || !o) return fail(NSA_ERR_INVALID, "null tensor pointer");
   if (batch < 0 || n_kv_heads <= 0) return fail(NSA_ERR_INVALID, "batch must be >= 0 and n_kv_heads > 0");
+  // an empty batch reads and writes nothing: its (empty) tensors may be NULL
+  if (batch > 0 && (!q || !k || !v || !o)) return fail(NSA_ERR_INVALID, "null tensor pointer");
   if (head_dim != kHeadDim) return fail(NSA_ERR_UNSUPPORTED, "head_dim must be 128 (got %lld)", (long long)head_dim);
   if (n_heads != n_kv_heads * kGroupHeads)
     return fail(NSA_ERR_UNSUPPORTED, "n_heads must be 8 * n_kv_heads (got %lld, %lld)", (long long)n_heads,
@@ -721,7 +728,8 @@ int nsa_ring_append(void* k_cache, void* v_cache, int64_t* unit_lens, const void
                     int64_t batch, int64_t n_kv_heads, int64_t head_dim, int64_t window, int64_t sink,
                     nsa_stream_t stream) {
   clear_error();
-  if (!k_cache || !v_cache || !unit_lens || !new_k || !new_v) return fail(NSA_ERR_INVALID, "null pointer");
+  if (batch > 0 && (!k_cache || !v_cache || !unit_lens || !new_k || !new_v))
+    return fail(NSA_ERR_INVALID, "null pointer");
   if (head_dim != kHeadDim) return fail(NSA_ERR_UNSUPPORTED, "head_dim must be 128");
   if (batch < 0 || n_kv_heads <= 0 || window < 0 || sink < 0 || window + sink < 1 ||
       window + sink > (int64_t(1) << 30))
@@ -741,7 +749,7 @@ int nsa_ring_decode(const void* q, const void* k_cache, const void* v_cache, voi
                     int64_t n_kv_heads, int64_t head_dim, int64_t window, int64_t sink, const int64_t* unit_lens,
                     float sm_scale, void* workspace, size_t workspace_bytes_, nsa_stream_t stream) {
   clear_error();
-  if (!unit_lens) return fail(NSA_ERR_INVALID, "unit_lens must not be NULL");
+  if (batch > 0 && !unit_lens) return fail(NSA_ERR_INVALID, "unit_lens must not be NULL");
   Params p{};
   int rc = sparse_params(q, k_cache, v_cache, o, batch, n_heads, n_kv_heads, head_dim, window, sink, sm_scale, p);
   if (rc) return rc;
@@ -755,7 +763,7 @@ int nsa_ring_decode_step(const void* q, void* k_cache, void* v_cache, void* o, i
                          const void* new_k, const void* new_v, float sm_scale, void* workspace,
                          size_t workspace_bytes_, nsa_stream_t stream) {
   clear_error();
-  if (!unit_lens || !new_k || !new_v) return fail(NSA_ERR_INVALID, "null pointer");
+  if (batch > 0 && (!unit_lens || !new_k || !new_v)) return fail(NSA_ERR_INVALID, "null pointer");
   if (!aligned16(new_k) || !aligned16(new_v)) return fail(NSA_ERR_ALIGN, "new_k and new_v must be 16-byte aligned");
   Params p{};
   int rc = sparse_params(q, k_cache, v_cache, o, batch, n_heads, n_kv_heads, head_dim, window, sink, sm_scale, p);

@@ -64,7 +64,7 @@ int pipe_call(nsa_host_pipe* p, const void* x_host, size_t in_need, void* o_host
               cudaStream_t stream, Decode&& decode) {
   int rc = check_pipe(p, in_need, out_need);
   if (rc) return rc;
-  if (!x_host || !o_host) return fail(NSA_ERR_INVALID, "null host buffer");
+  if ((in_need > 0 && !x_host) || (out_need > 0 && !o_host)) return fail(NSA_ERR_INVALID, "null host buffer");
   const int b = static_cast<int>(p->calls % p->depth);
   const bool reuse = p->calls >= static_cast<uint64_t>(p->depth);
   uint8_t* x_dev = p->dev + b * p->slot_bytes;

@@ -1194,6 +1194,7 @@ int kivi_check_stream_cache(const nsa_kivi_stream_cache& c) {
     return fail(NSA_ERR_INVALID, "window - residual must be a multiple of 32");
   const int64_t ng = c.window >= c.residual ? (c.window - c.residual) / 32 : 0;
   if (c.n_groups != ng) return fail(NSA_ERR_INVALID, "n_groups must be (window - residual) / 32");
+  if (c.batch == 0) return NSA_OK;  // an empty cache: its (empty) tensors may be NULL
   if (!c.unit_lens) return fail(NSA_ERR_INVALID, "unit_lens must not be NULL");
   if (!all_aligned({c.sink_k, c.sink_v, c.groups, c.k_res, c.v_res}))
     return fail(NSA_ERR_ALIGN, "stream cache tensors must be non-null and 16-byte aligned");
@@ -1230,9 +1231,10 @@ int nsa_kivi_decode(const void* q, const void* k_res, const void* v_res, const v
     return fail(NSA_ERR_INVALID, "need window >= residual >= 1 and (window - residual) %% 32 == 0 "
                                  "(build_quantized_kv_cache's assumption)");
   const int ng = static_cast<int>((window - residual) / 32);
-  if (!all_aligned({q, o, k_res, v_res, k_sink_packed, k_sink_scale, k_sink_zero, v_sink_packed, v_sink_scale,
-                    v_sink_zero}) ||
-      (ng > 0 && !all_aligned({k_win_packed, k_win_scale, k_win_zero, v_win_packed, v_win_scale, v_win_zero})))
+  if (batch > 0 &&  // an empty batch reads and writes nothing: its (empty) tensors may be NULL
+      (!all_aligned({q, o, k_res, v_res, k_sink_packed, k_sink_scale, k_sink_zero, v_sink_packed, v_sink_scale,
+                     v_sink_zero}) ||
+       (ng > 0 && !all_aligned({k_win_packed, k_win_scale, k_win_zero, v_win_packed, v_win_scale, v_win_zero}))))
     return fail(NSA_ERR_ALIGN, "all tensors must be non-null and 16-byte aligned");
   KParams p{};
   p.q = static_cast<const __half*>(q);
@@ -1311,7 +1313,7 @@ int nsa_kivi_stream_decode(const nsa_kivi_stream_cache* cache, const void* q, vo
   const nsa_kivi_stream_cache& c = *cache;
   int rc = kivi_check_stream_cache(c);
   if (rc) return rc;
-  if (!all_aligned({q, o})) return fail(NSA_ERR_ALIGN, "q and o must be non-null and 16-byte aligned");
+  if (c.batch > 0 && !all_aligned({q, o})) return fail(NSA_ERR_ALIGN, "q and o must be non-null and 16-byte aligned");
   KParams p;
   stream_params(c, q, o, sm_scale, p);
   return launch(p, stream_plan(c), c.k_res, c.v_res, workspace, workspace_bytes, stream);
@@ -1321,13 +1323,14 @@ int nsa_kivi_stream_decode_step(const nsa_kivi_stream_cache* cache, const void* 
                                 const void* q, void* o, float sm_scale, void* workspace, size_t workspace_bytes,
                                 nsa_stream_t stream) {
   clear_error();
-  if (!cache || !new_k || !new_v) return fail(NSA_ERR_INVALID, "null pointer");
+  if (!cache) return fail(NSA_ERR_INVALID, "null cache");
   const nsa_kivi_stream_cache& c = *cache;
   int rc = kivi_check_stream_cache(c);
   if (rc) return rc;
-  if (!all_aligned({q, o, new_k, new_v}))
+  if (c.batch > 0 && !all_aligned({q, o, new_k, new_v}))
     return fail(NSA_ERR_ALIGN, "q, o, new_k and new_v must be non-null and 16-byte aligned");
   const Plan s = stream_plan(c);
+  if (s.n_units == 0) return NSA_OK;
   if (s.ppu == 1 && fused_append_enabled()) {
     KParams p;
     stream_params(c, q, o, sm_scale, p);
@@ -1359,7 +1362,7 @@ int nsa_kivi_stream_decode_step_layers(const nsa_kivi_stream_cache* caches, int6
     if (c.batch != c0.batch || c.n_kv_heads != c0.n_kv_heads || c.window != c0.window || c.sink != c0.sink ||
         c.residual != c0.residual)
       return fail(NSA_ERR_INVALID, "all layers' caches must have the geometry of layer 0");
-    if (!all_aligned({q[l], o[l], new_k[l], new_v[l]}))
+    if (c.batch > 0 && !all_aligned({q[l], o[l], new_k[l], new_v[l]}))
       return fail(NSA_ERR_ALIGN, "q, o, new_k and new_v of every layer must be non-null and 16-byte aligned");
   }
   const Plan s = stream_plan(c0);

@@ -315,11 +315,11 @@ int nsa_kivi_dequant_k(const void* packed, const void* scale, const void* zero, 
                        int64_t n_kv_heads, int64_t seq_len, int64_t head_dim, int64_t tok_start, int64_t n_tokens,
                        nsa_stream_t stream) {
   clear_error();
-  if (!packed || !scale || !zero || !out) return fail(NSA_ERR_INVALID, "null tensor pointer");
   if (seq_len <= 0 || seq_len % 32 || n_tokens < 0 || head_dim <= 0)
     return fail(NSA_ERR_INVALID, "need seq_len > 0, seq_len % 32 == 0, n_tokens >= 0");
   const int64_t units = batch * n_kv_heads, total = units * n_tokens * head_dim;
   if (total == 0) return NSA_OK;
+  if (!packed || !scale || !zero || !out) return fail(NSA_ERR_INVALID, "null tensor pointer");
   dequant_k_kernel<<<grid_for(total, 256), 256, 0, stream>>>(
       static_cast<const uint8_t*>(packed), static_cast<const __half*>(scale), static_cast<const __half*>(zero),
       static_cast<float*>(out), units, seq_len, static_cast<int>(head_dim), tok_start, n_tokens);
@@ -331,11 +331,11 @@ int nsa_kivi_dequant_v(const void* packed, const void* scale, const void* zero, 
                        int64_t n_kv_heads, int64_t seq_len, int64_t head_dim, int64_t tok_start, int64_t n_tokens,
                        nsa_stream_t stream) {
   clear_error();
-  if (!packed || !scale || !zero || !out) return fail(NSA_ERR_INVALID, "null tensor pointer");
   if (seq_len <= 0 || n_tokens < 0 || head_dim <= 0 || head_dim % 32)
     return fail(NSA_ERR_INVALID, "need seq_len > 0, n_tokens >= 0, head_dim % 32 == 0");
   const int64_t units = batch * n_kv_heads, total = units * n_tokens * head_dim;
   if (total == 0) return NSA_OK;
+  if (!packed || !scale || !zero || !out) return fail(NSA_ERR_INVALID, "null tensor pointer");
   dequant_v_kernel<<<grid_for(total, 256), 256, 0, stream>>>(
       static_cast<const uint8_t*>(packed), static_cast<const __half*>(scale), static_cast<const __half*>(zero),
       static_cast<float*>(out), units, seq_len, static_cast<int>(head_dim), tok_start, n_tokens);
@@ -345,12 +345,13 @@ int nsa_kivi_dequant_v(const void* packed, const void* scale, const void* zero, 
 
 int nsa_kivi_append(const nsa_kivi_stream_cache* cache, const void* new_k, const void* new_v, nsa_stream_t stream) {
   clear_error();
-  if (!cache || !new_k || !new_v) return fail(NSA_ERR_INVALID, "null pointer");
+  if (!cache) return fail(NSA_ERR_INVALID, "null cache");
   const nsa_kivi_stream_cache& c = *cache;
   int rc = kivi_check_stream_cache(c);
   if (rc) return rc;
   const int64_t units = c.batch * c.n_kv_heads;
   if (units == 0) return NSA_OK;
+  if (!new_k || !new_v) return fail(NSA_ERR_INVALID, "null pointer");
   cudaError_t e = launch_kernel(
       kivi_append_kernel, dim3(static_cast<unsigned>(units)), dim3(128), 0, stream,
       static_cast<const __half*>(new_k), static_cast<const __half*>(new_v), static_cast<__half*>(c.sink_k),

@@ -59,6 +59,10 @@ def test_workspace_queries_without_gpu(lib):
     assert L.nsa_dense_workspace_bytes(32, 8, 8192) > 0
     assert L.nsa_sparse_workspace_bytes(32, 8, 256, 4) > 0
     assert L.nsa_dense_workspace_bytes(-1, 8, 10) == 0
+    # an empty batch is a valid (no-op) call: its queries return without work
+    assert L.nsa_dense_workspace_bytes(0, 8, 8192) < 4096
+    assert L.nsa_sparse_workspace_bytes(0, 8, 256, 4) < 4096
+    assert L.nsa_kivi_workspace_bytes(0, 8, 256, 128) < 4096
 
 
 def test_host_validation_rejects_cpu_tensors():
