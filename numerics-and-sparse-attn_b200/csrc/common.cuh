@@ -121,6 +121,12 @@ __device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int c0, 
                "r"(c0), "r"(c1), "r"(c2), "r"(c3)
                : "memory");
 }
+// Prefetch [src, src + bytes) into L2 (16-byte aligned, a multiple of 16
+// bytes): no shared memory, no completion; a later load of the range then
+// waits on L2 instead of DRAM.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 // Add `bytes` to the transaction count of the current phase without arriving.
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");

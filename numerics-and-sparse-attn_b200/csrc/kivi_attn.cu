@@ -780,7 +780,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   grid_launch_dependents();
   // the cache and q may come from the previous kernel of the stream: global
-  // memory is touched only after the wait below (the barriers are initialised
+  // memory is read only after the wait below (the barriers are initialised
   // first, which measured 0.25 us faster per step launch)
   if (smem_u32(smem_raw) & 1023u) {  // TMA tile destinations need 1024-byte alignment
     if (threadIdx.x == 0) set_error(p.err, NSA_ERR_ALIGN);
@@ -810,6 +810,13 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
     fence_barrier_init();
   }
   __syncthreads();
+  // Batch 0 goes to L2 while the previous grid finishes (a prefetch reads
+  // nothing into this CTA, and L2 stays coherent with that grid's writes), so
+  // its copy after the wait lands sooner: -0.5 us per attention launch, -0.3
+  // per step.  Prefetching the residual tiles as well measured 0.8 us slower.
+  if (kRec && has_b0 && threadIdx.x == 0)
+    bulk_prefetch_l2(p.grp + unit * (p.n_groups + 1) * int64_t(kRecBytes),
+                     static_cast<uint32_t>(min(p.n_groups + 1, kBatchGroups)) * kRecBytes);
   grid_dependency_wait();
 
   // ------------------------------------------------------------- prologue
