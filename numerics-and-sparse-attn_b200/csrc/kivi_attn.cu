@@ -125,6 +125,7 @@ static_assert(offsetof(Smem, f) == 0 && kFStageBytes % 1024 == 0 && kFRegion % 1
 static_assert(offsetof(Smem, qb) % 16 == 0 && kQStageBytes % 16 == 0, "bulk-copy destinations");
 static_assert(offsetof(Smem, qpad) % 16 == 0 && (kQPadStride * 2) % 16 == 0, "16-byte stores");
 static_assert(sizeof(EpilogueSmem) <= sizeof(uint8_t[kFStages][kFStageBytes]), "epilogue alias");
+static_assert(kFStages < kCWarps, "warps 1..kFStages issue the first F-tiles");
 // The dynamic shared-memory window of a CTA starts 1024-byte aligned on sm_100
 // (the kernel checks it); 1 KiB per CTA is reserved by the system.
 constexpr size_t kSmemBytes = sizeof(Smem);
@@ -667,10 +668,11 @@ __device__ __noinline__ void quantize_flushed_group(const KParams& p, int64_t un
   store_group_record(x, y, qs, sl, group_rec(p.grp, unit, p.n_groups, 1 + gs), c);
 }
 
-// Load issue, run by lane 0 of warp 0.  Each ring is filled in order; an
-// item is issued once warp 0 itself has consumed the previous user of its
-// stage (the other warps' release is then waited for, which never depends on
-// an item not yet issued).
+// Load issue, run by lane 0 of warp 0 (at launch start, the F-tiles of the
+// free stages by lanes 0 of warps 1..kFStages).  Each ring is filled in
+// order; an item is issued once warp 0 itself has consumed the previous user
+// of its stage (the other warps' release is then waited for, which never
+// depends on an item not yet issued).
 template <bool kRec>
 struct Issuer {
   const KParams& p;
@@ -750,6 +752,34 @@ struct Issuer {
       }
       ++f_issued;
       ++f_next;
+    }
+  }
+  // F-tile f_next + i into stage i, free at launch start (no wait), by any thread.
+  __device__ __forceinline__ void first_f(int i) {
+    const int f = f_next + i;
+    if (f >= f_end) return;
+    const uint32_t fb = smem_u32(&sm.f_full[i]);
+    const uint32_t sd = smem_u32(sm.f[i]);
+    if constexpr (kRec) {
+      const int row0 = f * kFRows;
+      const uint32_t rows = static_cast<uint32_t>(min(kFRows, p.res_cap - row0));
+      mbar_arrive_expect_tx(fb, 2 * rows * 256);
+      const int64_t off = (unit * p.res_cap + row0) * kHeadDim;
+      bulk_load(sd, p.k_res + off, rows * 256, fb);
+      bulk_load(sd + kFTile, p.v_res + off, rows * 256, fb);
+    } else {
+      mbar_arrive_expect_tx(fb, kFStageBytes);
+      const int uu = static_cast<int>(unit);
+      tma_load_4d(sd, tmK, fb, 0, f * kFRows, 0, uu);
+      tma_load_4d(sd + kFTile, tmV, fb, 0, f * kFRows, 0, uu);
+    }
+  }
+  // The leader's account of the tiles first_f issued.
+  __device__ __forceinline__ void skip_first_f() {
+    const int n = min(kFStages, f_end - f_next);
+    if (n > 0) {
+      f_issued += n;
+      f_next += n;
     }
   }
   // Live Q-batches after the first, likewise (q_cons Q-batches consumed).
@@ -844,8 +874,11 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
       prefetch_tmap(tmV);
     }
     if (has_b0) iss.batch0();
-    iss.pump_f(0);
+    iss.skip_first_f();
   }
+  // the free stages' F-tiles, one warp each: their copies are issued while lane 0 of warp 0
+  // issues batch 0 (each copy request takes hundreds of cycles to issue): -0.1 to -0.2 us
+  if (lane == 0 && warp >= 1 && warp <= kFStages) iss.first_f(warp - 1);
   int len = static_cast<int>(len64);
   if (kRec && (len64 < 0 || len64 >= kMaxUnitLen)) {  // outside what the 32-bit ring arithmetic covers
     if (threadIdx.x == 0) set_error(p.err, NSA_ERR_INVALID);
