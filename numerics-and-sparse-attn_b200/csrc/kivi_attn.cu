@@ -26,9 +26,12 @@
 // batch 0, residual) are issued before that length is read.  Q-batches after
 // the first that hold no attended token are skipped by every warp alike.
 //
-// Warps 0-3 consume, taking jobs (a quantized group, or 16 rows of an F-tile)
-// by a static cost-balanced assignment that every warp computes alike; lane 0
-// of warp 0 also issues the loads.  With no separate producer warp, a CTA is 4
+// Warps 0-3 consume, each claiming the next job of the staged item (a
+// quantized group, or 32 rows of an F-tile) from a shared-memory counter as
+// soon as it is free, so the work follows the warps' real progress (the
+// order in which a unit's partial sums accumulate, and so the output's last
+// rounding, can differ between launches; the cache state cannot); lane 0 of
+// warp 0 also issues the loads.  With no separate producer warp, a CTA is 4
 // warps and two CTAs per SM leave up to 255 registers per thread, which the
 // dequantization's independent chains need to overlap.  A quantized group is dequantized in
 // registers straight into mma.sync fragments, with no shared-memory round trip:
@@ -119,6 +122,7 @@ struct Smem {
   uint64_t f_full[kFStages], f_empty[kFStages];
   uint64_t q_full[kQStages], q_empty[kQStages];
   int q_rel[kQStages];  // warps that have released the stage's current Q-batch
+  int f_job[kFStages], q_job[kQStages], d_job;  // next job of the staged item (claimed by warps)
 };
 
 static_assert(offsetof(Smem, f) == 0 && kFStageBytes % 1024 == 0 && kFRegion % 1024 == 0, "TMA tile destinations");
@@ -249,30 +253,17 @@ __device__ __forceinline__ bool batch_live(const KParams& p, const KiviMeta& m, 
   return false;
 }
 
-// Static job assignment: each job goes to the consumer warp with the least
-// estimated work so far (all warps run the same sequence, so they agree).
-struct JobSched {
-  int cost[kCWarps];
-  __device__ __forceinline__ JobSched() {
-#pragma unroll
-    for (int w = 0; w < kCWarps; ++w) cost[w] = 0;
-  }
-  __device__ __forceinline__ int take(int c) {
-    int best = 0, bc = cost[0];
-#pragma unroll
-    for (int w = 1; w < kCWarps; ++w)
-      if (cost[w] < bc) {
-        bc = cost[w];
-        best = w;
-      }
-#pragma unroll
-    for (int w = 0; w < kCWarps; ++w) cost[w] += (w == best) ? c : 0;  // static indexing: stays in registers
-    return best;
-  }
-};
-constexpr int kCostF = 1;           // 16 fp16 residual rows
-constexpr int kCostGroup = 2;       // per quantized group (query scaling, zero-point term)
-constexpr int kCostGroupHalf = 3;   // per 16 attended-token half of a quantized group
+// Dynamic job assignment: the jobs of a staged item (the groups of a
+// Q-batch, the 32-row slices of an F-tile) are claimed in order from a
+// shared-memory counter by whichever warp is free first; lane 0 claims for
+// its warp.  The counter is reset when the stage is refilled (after every
+// warp has released it, before the refill's barrier arrival publishes it).
+constexpr int kFJobs = (kFRows + 31) / 32;
+__device__ __forceinline__ int claim_job(int* counter, int lane) {
+  int j = 0;
+  if (lane == 0) j = atomicAdd(counter, 1);
+  return __shfl_sync(0xffffffffu, j, 0);
+}
 
 // ---------------------------------------------------------------- registers
 __device__ __forceinline__ __half2 u32_as_h2(uint32_t x) { return *reinterpret_cast<__half2*>(&x); }
@@ -737,6 +728,7 @@ struct Issuer {
       }
       const uint32_t fb = smem_u32(&sm.f_full[s]);
       const uint32_t sd = smem_u32(sm.f[s]);
+      sm.f_job[s] = 0;  // every warp has released the stage
       if constexpr (kRec) {  // rows f_next*80 .. of the unit's ring, K and V one copy each
         const int row0 = f_next * kFRows;
         const uint32_t rows = static_cast<uint32_t>(min(kFRows, p.res_cap - row0));
@@ -836,7 +828,10 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
       mbar_init(smem_u32(&sm.q_full[s]), 1);
       mbar_init(smem_u32(&sm.q_empty[s]), kCWarps);
       sm.q_rel[s] = 0;
+      sm.q_job[s] = 0;
     }
+    for (int s = 0; s < kFStages; ++s) sm.f_job[s] = 0;
+    sm.d_job = 0;
     fence_barrier_init();
   }
   __syncthreads();
@@ -905,7 +900,6 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   st.reset();
   const uint32_t qpad = smem_u32(sm.qpad);
   const uint32_t qrow = qpad + g * (kQPadStride * 2) + 32 * t;
-  JobSched js;
   uint32_t nf = 0, nq = 0;
   // Steps: 0 = Q-batch 0, 1 = the F-tiles, 2 = Q-batches b_begin .., 3 = the
   // deferred slot below (one loop, so that each consumer path -- attend_group
@@ -931,9 +925,11 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
         ++nf;
         if (!aborted && !mbar_wait(smem_u32(&sm.f_full[s]), ph, p.err)) aborted = true;
         const uint32_t sd = smem_u32(sm.f[s]);
-        // jobs of 32 rows (the last one 16): one softmax step per job
+        // jobs of 32 rows (the last one 16): one softmax step per job, each
+        // claimed by the first warp free to take it
 #pragma unroll 1
-        for (int r = 0; r < kFRows; r += 32) {
+        for (int j = claim_job(&sm.f_job[s], lane); j < kFJobs; j = claim_job(&sm.f_job[s], lane)) {
+          const int r = 32 * j;
           const int r0 = f * kFRows + r;
           const bool two = r + 32 <= kFRows;
           bool vl[2], vh[2];
@@ -945,7 +941,6 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
           const bool any0 = __any_sync(0xffffffffu, vl[0] || vh[0]);
           const bool any1 = __any_sync(0xffffffffu, vl[1] || vh[1]);
           if (!any0 && !any1) continue;
-          if (js.take(kCostF * ((any0 ? 1 : 0) + (any1 ? 1 : 0))) != warp) continue;
           if (ap.f_item == f && ap.f_row >= r && ap.f_row < r + (two ? 32 : 16))  // the appended token's
             patch_residual_row(sd, ap.f_row, smem_u32(sm.newtok), lane);      // staged row is stale
           st.load_q(qpad, lane, kQPadStride * 2);  // reloaded here: not held across the quantized path
@@ -1003,13 +998,12 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
         quantize_flushed_group(p, unit, ap.fl_base, ap.fl_gs, qs, ap.fl_slot, smem_u32(sm.f[0]), ct);
         cwarps_sync();
       }
+      int* const jobs = phase == 3 ? &sm.d_job : &sm.q_job[s];  // each group claimed by the first free warp
 #pragma unroll 1
-      for (int gs = 0; gs < kBatchGroups; ++gs) {
+      for (int gs = claim_job(jobs, lane); gs < kBatchGroups; gs = claim_job(jobs, lane)) {
         if (phase == 3 ? gs != ap.fl_slot : (defer_slot && b == 0 && gs == ap.fl_slot)) continue;
         const uint32_t mask = group_mask(p, meta, b, gs);
         if (!mask) continue;
-        const int halves = ((mask & 0xffffu) ? 1 : 0) + ((mask >> 16) ? 1 : 0);
-        if (js.take(kCostGroup + kCostGroupHalf * halves) != warp) continue;
         attend_group<kRec>(st, qrow, lq, qs, gs, mask, p.scale_log2, lane);
       }
       if (phase != 3) {  // release the stage; the last warp to do so refills it
@@ -1018,6 +1012,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
           __threadfence_block();  // this warp's reads of the stage come first
           if (atomicAdd(&sm.q_rel[s], 1) == kCWarps - 1) {
             sm.q_rel[s] = 0;
+            sm.q_job[s] = 0;  // every warp has stopped claiming from this batch
             __threadfence_block();
             // the stage's next batch is two live batches on in the issue order
             // (batch 0, then the live batches from b_begin)

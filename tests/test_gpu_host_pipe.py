@@ -1,9 +1,10 @@
 """Host-buffer entry points (HostPipe + *_host calls): the query and output in
 pinned host memory, copies and decode pipelined on a two-slot pipe.  Every
-output equals the device-tensor call on the same inputs bit for bit, over
-enough calls that each slot is reused (and, for KIVI, across a group flush),
-and the KIVI cache state after host-buffer steps equals that after device
-steps."""
+output equals the device-tensor call on the same inputs (bit for bit on the
+fp16 paths; up to rounding for KIVI, whose warps take a unit's jobs in
+whichever order they free up), over enough calls that each slot is reused
+(and, for KIVI, across a group flush), and the KIVI cache state after
+host-buffer steps equals that after device steps bit for bit."""
 import importlib
 
 import pytest
@@ -39,7 +40,7 @@ def test_kivi_step_host_equals_device_step():
     ref = [dev_cache.decode_step(qs[i], ks[i], vs[i]).cpu() for i in range(n_steps)]
     torch.cuda.synchronize()
     for i in range(n_steps):
-        assert torch.equal(outs[i], ref[i]), f"step {i}"
+        assert (outs[i].float() - ref[i].float()).abs().max().item() < 2e-3, f"step {i}"
     a, b = dev_cache.state(), host_cache.state()
     for key in a:
         assert torch.equal(a[key], b[key]), key

@@ -261,10 +261,10 @@ def test_fused_step_equals_append_then_attend(W):
     """B=32 (every unit gets its own CTA): the one-launch decode step --
     store, group flush or sink re-quantization and attention in the decode
     kernel -- gives cache states bit-identical to nsa_kivi_append followed by
-    nsa_kivi_stream_decode, and the same outputs (bit-identical except on
-    group-flush steps, whose item order differs: rounding-level there), from an
-    empty cache through the sink phase, the first flushes (dropped groups when
-    W == R) and eviction."""
+    nsa_kivi_stream_decode, and the same outputs up to rounding (a unit's jobs
+    go to whichever warp is free first, so the order in which partial sums are
+    accumulated varies between launches), from an empty cache through the sink
+    phase, the first flushes (dropped groups when W == R) and eviction."""
     B, Hkv, S, R = 32, 8, 4, 128
     n_steps = S + max(W, R + 32) + R + 2 * 32 + 3
     g = torch.Generator(device=DEV).manual_seed(70 + W)
@@ -279,12 +279,7 @@ def test_fused_step_equals_append_then_attend(W):
         o_f = fused.decode_step(q, nk, nv)
         split.append(nk, nv)
         o_s = split.attend(q)
-        if L > S + R and (L - S - R) % 32 == 0:
-            # this append flushes a group: the launch visits its items in another
-            # order, so the result may differ in rounding (the state may not)
-            assert _err(o_f, o_s) < 2e-3, L
-        else:
-            assert torch.equal(o_f, o_s), L
+        assert _err(o_f, o_s) < 2e-3, L  # rounding-level (accumulation order); the state is exact
         if L in check_at:
             a, b = _state_np(fused), _state_np(split)
             for key in a:
@@ -294,8 +289,8 @@ def test_fused_step_equals_append_then_attend(W):
 def test_fused_step_multi_batch_window():
     """W=1024 (28 window groups: six Q-batches refilled through the two-stage
     ring while the warps work): fused decode steps across a group flush match
-    the oracle, give append + attend's outputs (bit for bit off flush steps)
-    and leave the same cache state."""
+    the oracle, give append + attend's outputs up to rounding and leave the
+    same cache state (bit for bit)."""
     B, Hkv, W, L, S, R = 32, 8, 1024, 163_840, 4, 128
     fused = quant_kernel.KiviCache.synthetic(B, Hkv, W, L, device=DEV,
                                              generator=torch.Generator(device=DEV).manual_seed(9))
@@ -311,10 +306,7 @@ def test_fused_step_multi_batch_window():
         o_f = fused.decode_step(q, nk, nv)
         split.append(nk, nv)
         o_s = split.attend(q)
-        if (L + step - S + 1 - R) % 32 == 0:  # this append flushes a group
-            assert _err(o_f, o_s) < 2e-3, step
-        else:
-            assert torch.equal(o_f, o_s), step
+        assert _err(o_f, o_s) < 2e-3, step  # rounding-level (accumulation order)
         if step in (0, 27, 28, 35):
             ref = oa.stream_attention(q, _state_np(fused), L + step + 1, geom)
             assert _err(o_f, ref) < TOL_2BIT, step
@@ -323,10 +315,41 @@ def test_fused_step_multi_batch_window():
         np.testing.assert_array_equal(a[key], b[key], err_msg=key)
 
 
+@pytest.mark.parametrize("R,W", [(256, 512), (384, 384)])
+def test_large_residual_ring_refills_residual_stages(R, W):
+    """A residual ring of R + 32 = 288 / 416 slots is four / six F-tiles, more
+    than the two F stages: the tiles are refilled into freed stages while the
+    warps work (and the job counters reset with them).  Fused steps across a
+    group flush match the oracle and append + attend, and the state stays
+    bit-exact with append + attend."""
+    B, Hkv, L, S = 32, 8, 100_000, 4
+    mk = lambda: quant_kernel.KiviCache.synthetic(B, Hkv, W, L, residual=R, device=DEV,  # noqa: E731
+                                                  generator=torch.Generator(device=DEV).manual_seed(31))
+    fused, split = mk(), mk()
+    assert fused.step_launches() == 1
+    geom = ok.StreamGeometry(window=W, sink=S, residual=R)
+    g = torch.Generator(device=DEV).manual_seed(32)
+    for step in range(34):
+        q = torch.randn(B, 64, 128, device=DEV, generator=g).half()
+        nk = torch.randn(B, Hkv, 128, device=DEV, generator=g).half()
+        nv = torch.randn(B, Hkv, 128, device=DEV, generator=g).half()
+        o_f = fused.decode_step(q, nk, nv)
+        split.append(nk, nv)
+        o_s = split.attend(q)
+        assert _err(o_f, o_s) < 2e-3, step
+        if step in (0, 5, 17, 33) or (L + step + 1 - S - R) % 32 == 0:
+            ref = oa.stream_attention(q, _state_np(fused), L + step + 1, geom)
+            assert _err(o_f, ref) < TOL_2BIT, step
+    a, b = _state_np(fused), _state_np(split)
+    for key in a:
+        np.testing.assert_array_equal(a[key], b[key], err_msg=key)
+
+
 def test_layer_batched_step_equals_per_layer_steps():
-    """decode_step_layers (3 layers in one launch) gives the same outputs and
-    cache states, bit for bit, as KiviCache.decode_step layer by layer, over
-    steps that include a group flush."""
+    """decode_step_layers (3 layers in one launch) gives the same cache states,
+    bit for bit, and the same outputs up to rounding (accumulation order) as
+    KiviCache.decode_step layer by layer, over steps that include a group
+    flush."""
     import importlib
     kivi = importlib.import_module("numerics-and-sparse-attn_b200.kivi")
     B, Hkv, W, L, n = 32, 8, 256, 163_840, 3
@@ -344,7 +367,7 @@ def test_layer_batched_step_equals_per_layer_steps():
         outs = kivi.decode_step_layers(batched, qs, nks, nvs)
         for layer in range(n):
             ref = single[layer].decode_step(qs[layer], nks[layer], nvs[layer])
-            assert torch.equal(outs[layer], ref), (step, layer)
+            assert _err(outs[layer], ref) < 2e-3, (step, layer)
     for a, b in zip(batched, single):
         sa, sb = _state_np(a), _state_np(b)
         for key in sa:
