@@ -314,8 +314,8 @@ constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 // once.  The unit's S+W slots come in 96-slot tiles, K and V each as one TMA
 // box holding both 64-dim halves (2-stage ring: 192 slots in flight, the rest
 // as soon as the first tile is consumed); lane 0 of warp 0 issues them.  Warps
-// take 32-slot jobs round-robin and run the shared fp16 engine; the epilogue
-// merges the 4 warps (its buffers reuse the ring).
+// claim 32-slot jobs as they free up (wclaim) and run the shared fp16 engine;
+// the epilogue merges the 4 warps (its buffers reuse the ring).
 namespace win {
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
@@ -334,6 +334,7 @@ struct Smem {
   __half qpad[kGroupHeads][kQPad];
   __half newtok[2][kHeadDim];  // appended token's K and V
   uint64_t full[kStages], empty[kStages];
+  int job[kStages];  // next 32-slot job of the staged tile
 };
 static_assert(offsetof(Smem, kv) == 0 && kStageB % 1024 == 0 && kRegion % 1024 == 0, "TMA tile destinations");
 static_assert(sizeof(EpilogueSmem) <= sizeof(uint8_t[kStages][kStageB]), "epilogue alias");
@@ -342,6 +343,15 @@ static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
 __device__ __forceinline__ void sync4() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
 }  // namespace win
 
+// The next 32-slot job of a staged tile, claimed by lane 0 for its warp from
+// the stage's counter (reset when the stage is refilled): whichever warp is
+// free first takes it, so the order in which a unit's partial sums accumulate
+// (and the output's last rounding) can differ between launches.
+__device__ __forceinline__ int wclaim(int* c, int lane) {
+  int j = 0;
+  if (lane == 0) j = atomicAdd(c, 1);
+  return __shfl_sync(0xffffffffu, j, 0);
+}
 __global__ void __launch_bounds__(win::kThreads, 2)
     window_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                          const Params p) {
@@ -363,6 +373,7 @@ __global__ void __launch_bounds__(win::kThreads, 2)
     for (int s = 0; s < win::kStages; ++s) {
       mbar_init(smem_u32(&sm.full[s]), 1);
       mbar_init(smem_u32(&sm.empty[s]), win::kWarps);
+      sm.job[s] = 0;
     }
     fence_barrier_init();
   }
@@ -390,6 +401,7 @@ __global__ void __launch_bounds__(win::kThreads, 2)
         break;
       }
       const uint32_t fb = smem_u32(&sm.full[s]), sd = smem_u32(sm.kv[s]);
+      sm.job[s] = 0;
       mbar_arrive_expect_tx(fb, win::kStageB);
       tma_load_4d(sd, &tmK, fb, 0, issued * win::kRows, 0, static_cast<int>(unit));
       tma_load_4d(sd + win::kTile, &tmV, fb, 0, issued * win::kRows, 0, static_cast<int>(unit));
@@ -424,7 +436,6 @@ __global__ void __launch_bounds__(win::kThreads, 2)
   st.reset();
   st.load_q(smem_u32(sm.qpad), lane, win::kQPad * 2);
   bool aborted = false;
-  uint32_t job = 0;
   for (int ti = 0; ti < n_tiles; ++ti) {
     if (leader) pump(ti);
     __syncwarp();
@@ -432,7 +443,8 @@ __global__ void __launch_bounds__(win::kThreads, 2)
     if (!aborted && !mbar_wait(smem_u32(&sm.full[s]), ph, p.err)) aborted = true;
     const uint32_t sd = smem_u32(sm.kv[s]);
 #pragma unroll 1
-    for (int r = 0; r < win::kRows; r += 32) {
+    for (int jj = wclaim(&sm.job[s], lane); jj < win::kRows / 32; jj = wclaim(&sm.job[s], lane)) {
+      const int r = 32 * jj;
       const int64_t r0 = int64_t(ti) * win::kRows + r;
       bool vl[2], vh[2];
 #pragma unroll
@@ -443,7 +455,6 @@ __global__ void __launch_bounds__(win::kThreads, 2)
       const bool any0 = __any_sync(0xffffffffu, vl[0] || vh[0]);
       const bool any1 = __any_sync(0xffffffffu, vl[1] || vh[1]);
       if (!any0 && !any1) continue;
-      if ((job++ % win::kWarps) != static_cast<uint32_t>(warp)) continue;
       if (aslot >= r0 && aslot < r0 + 32) {  // the appended token's staged row is stale
         const int row = aslot - ti * win::kRows, kv = lane >> 4, chunk = lane & 15;
         uint4 x = *reinterpret_cast<const uint4*>(&sm.newtok[kv][chunk * 8]);

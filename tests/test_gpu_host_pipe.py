@@ -1,8 +1,8 @@
 """Host-buffer entry points (HostPipe + *_host calls): the query and output in
 pinned host memory, copies and decode pipelined on a two-slot pipe.  Every
 output equals the device-tensor call on the same inputs (bit for bit on the
-fp16 paths; up to rounding for KIVI, whose warps take a unit's jobs in
-whichever order they free up), over enough calls that each slot is reused
+dense path; up to the last rounding for sink+window and KIVI, whose warps take
+a unit's jobs in whichever order they free up), over enough calls that each slot is reused
 (and, for KIVI, across a group flush), and the KIVI cache state after
 host-buffer steps equals that after device steps bit for bit."""
 import importlib
@@ -73,7 +73,10 @@ def test_fp16_host_equals_device(path):
             ref = pkg.sparse_decode_attention(qs[i], k, v, L, W, S, ring_head=heads)
         else:
             ref = pkg.dense_decode_attention(qs[i], k, v, slots - 5)
-        assert torch.equal(o_h[i], ref.cpu()), f"call {i}"
+        if path == "dense":
+            assert torch.equal(o_h[i], ref.cpu()), f"call {i}"
+        else:
+            assert (o_h[i].float() - ref.cpu().float()).abs().max().item() < 2e-3, f"call {i}"
     pipe.close()
 
 

@@ -3,7 +3,9 @@ cache contents after every append are the history's positions in their ring
 slots, and attention equals the oracle's sink+window attention over the same
 slots (sparse_kernel.py:15-46 slot rule with the ring head), through the sink
 phase, the first window fill and wrap-around; the one-launch step (B=32: every
-unit has its own CTA) equals append + decode bit for bit."""
+unit has its own CTA) leaves the cache of append + decode bit for bit and the
+same outputs up to the last rounding (the window kernel's warps claim a unit's
+jobs as they free up, so the accumulation order varies between launches)."""
 import importlib
 
 import pytest
@@ -66,7 +68,7 @@ def test_ring_fused_step_equals_append_then_attend():
         o_f = fused.decode_step(q, nk, nv)
         split.append(nk, nv)
         o_s = split.attend(q)
-        assert torch.equal(o_f, o_s), L
+        assert (o_f.float() - o_s.float()).abs().max().item() < 2e-3, L  # rounding-level
     assert torch.equal(fused.k, split.k) and torch.equal(fused.v, split.v)
     assert torch.equal(fused.unit_lens, split.unit_lens)
 
