@@ -352,6 +352,9 @@ __device__ __forceinline__ int wclaim(int* c, int lane) {
   if (lane == 0) j = atomicAdd(c, 1);
   return __shfl_sync(0xffffffffu, j, 0);
 }
+// kAppend: the launch also appends new_k / new_v (p.new_k non-null); two
+// instantiations, so that attention alone carries none of the append code.
+template <bool kAppend>
 __global__ void __launch_bounds__(win::kThreads, 2)
     window_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                          const Params p) {
@@ -360,7 +363,7 @@ __global__ void __launch_bounds__(win::kThreads, 2)
   // the cache and q may come from the previous kernel of the stream: global
   // memory is read only after the wait below (the barriers are initialised
   // first, which measured faster for attention alone and for append + attend)
-  const bool appending = p.new_k != nullptr;
+  constexpr bool appending = kAppend;
   if (smem_u32(smem_raw) & 1023u) {  // TMA tile destinations need 1024-byte alignment
     if (threadIdx.x == 0) set_error(p.err, NSA_ERR_ALIGN);
     return;
@@ -415,17 +418,22 @@ __global__ void __launch_bounds__(win::kThreads, 2)
   // whose job holds it, the cache slot and the length are stored at the end
   int64_t pos = 0;
   int aslot = -1;
-  if (appending) {
+  __half nk = __float2half_rn(0.f), nv = nk;
+  if (appending) {  // the loads go out now; their results are used once the tiles are issued
     pos = p.unit_lens[unit];
-    aslot = pos < p.sink ? static_cast<int>(pos)
-                         : (p.window > 0 ? p.sink + static_cast<int>((pos - p.sink) % p.window) : -1);
-    sm.newtok[0][ct] = p.new_k[unit * kHeadDim + ct];
-    sm.newtok[1][ct] = p.new_v[unit * kHeadDim + ct];
+    nk = p.new_k[unit * kHeadDim + ct];
+    nv = p.new_v[unit * kHeadDim + ct];
   }
   if (leader) {
     prefetch_tmap(&tmK);
     prefetch_tmap(&tmV);
     pump(0);
+  }
+  if (appending) {  // (using them before the issue measured 1.06 us slower per step)
+    aslot = pos < p.sink ? static_cast<int>(pos)
+                         : (p.window > 0 ? p.sink + static_cast<int>((pos - p.sink) % p.window) : -1);
+    sm.newtok[0][ct] = nk;
+    sm.newtok[1][ct] = nv;
   }
   const PieceMeta meta = make_meta(p, unit);
   asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(smem_u32(&sm.qpad[ct >> 4][(ct & 15) * 8])),
@@ -539,13 +547,18 @@ int launch_window(Params& p, int64_t n_units, const void* k, const void* v, int6
   static bool attr_set[64] = {false};
   const int dev = current_device().device;
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(window_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(window_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(win::kSmem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(window_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(win::kSmem));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     attr_set[dev] = true;
   }
-  cudaError_t e = launch_kernel(window_decode_kernel, dim3(static_cast<unsigned>(n_units)), dim3(win::kThreads),
-                                win::kSmem, stream, mk, mv, p);
+  cudaError_t e = p.new_k ? launch_kernel(window_decode_kernel<true>, dim3(static_cast<unsigned>(n_units)),
+                                          dim3(win::kThreads), win::kSmem, stream, mk, mv, p)
+                          : launch_kernel(window_decode_kernel<false>, dim3(static_cast<unsigned>(n_units)),
+                                          dim3(win::kThreads), win::kSmem, stream, mk, mv, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "window_decode_kernel launch");
   return NSA_OK;
