@@ -67,7 +67,7 @@ def algorithmic_bytes(workload: str, batch: int) -> int:
 # dominant kernel at B=32, from the committed ncu captures of this exact workload.
 NCU_TRAFFIC = {
     "kivi": (25_626_624, "profiles/kivi_stream_step_kernel_kivi_W256_L163840_B32.md"),
-    "sparse": (34_634_240, "profiles/window_decode_kernel_sparse_W256_L163840_B32.md"),
+    "sparse": (34_632_960, "profiles/window_decode_kernel_sparse_W256_L163840_B32.md"),
     "dense": (1_078_491_176, "profiles/fp16_decode_kernel_dense_L8192_B32.md"),
 }
 
