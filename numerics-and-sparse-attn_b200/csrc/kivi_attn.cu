@@ -869,11 +869,15 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
       prefetch_tmap(tmV);
     }
     if (has_b0) iss.batch0();
-    iss.skip_first_f();
+    if constexpr (kRec)
+      iss.skip_first_f();
+    else
+      iss.pump_f(0);
   }
-  // the free stages' F-tiles, one warp each: their copies are issued while lane 0 of warp 0
-  // issues batch 0 (each copy request takes hundreds of cycles to issue): -0.1 to -0.2 us
-  if (lane == 0 && warp >= 1 && warp <= kFStages) iss.first_f(warp - 1);
+  // streaming layout: the free stages' F-tiles, one warp each: their copies are issued while
+  // lane 0 of warp 0 issues batch 0 (each copy request takes hundreds of cycles to issue):
+  // -0.1 to -0.2 us.  (The reference layout's tile loads need the tensor maps lane 0 prefetches.)
+  if (kRec && lane == 0 && warp >= 1 && warp <= kFStages) iss.first_f(warp - 1);
   int len = static_cast<int>(len64);
   if (kRec && (len64 < 0 || len64 >= kMaxUnitLen)) {  // outside what the 32-bit ring arithmetic covers
     if (threadIdx.x == 0) set_error(p.err, NSA_ERR_INVALID);
