@@ -18,6 +18,12 @@
  * batch (B = 0) launches nothing and returns NSA_OK; its tensor pointers may
  * then be NULL (what zero-size tensors carry).
  *
+ * Reproducibility: the sink+window and KIVI attention kernels let their warps
+ * claim a unit's work as they free up, so the order in which partial sums are
+ * accumulated -- and with it the last fp16 rounding of an output -- can differ
+ * between launches on the same inputs.  Cache contents written by the append
+ * and quantization paths are bit-exact; the dense path is deterministic.
+ *
  * Errors: argument problems are reported synchronously (NSA_ERR_INVALID,
  * NSA_ERR_ALIGN, NSA_ERR_UNSUPPORTED, NSA_ERR_WORKSPACE) with a message from
  * nsa_last_error_message(); launch failures as NSA_ERR_CUDA.  Kernels never
