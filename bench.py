@@ -1,25 +1,37 @@
 """Decode-attention benchmark (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload kivi|sparse|dense]
-                    [--impl ours|reference]
+                    [--impl ours|reference] [--no-cpu-baseline] [--headline-only]
 
 A step is one decode-attention pass (one query token per sequence, one layer)
 over a batch of B=32 sequences per GPU with 64 query / 8 KV heads, d=128:
 
-* ``kivi``   (default) KIVI 2-bit sink+window cache,
+* ``kivi``   (default, the headline) KIVI 2-bit sink+window cache, S=4,
              W=256, after L=163,840 appended tokens; the step appends one new
              token per sequence (quantize-on-append) and attends.
-* ``sparse`` (config 3) fp16 sink+window ring cache, W=256, L=163,840.
-* ``dense``  (config 2) dense fp16 cache, L=8,192.
+* ``sparse`` fp16 sink+window ring cache, S=4, W=256, L=163,840.
+* ``dense``  dense fp16 cache, L=8,192.
 
 Inputs: seeded N(0,1) fp16 on the device (K with 4 of 128 channels x8 for
 KIVI).  L2 honesty: each step reads a different layer's cache from a rotation
-whose total size exceeds the 126 MB L2, like successive layers of a model.
-``value`` = sequences decoded per second over all GPUs (tokens/s), timed on
-the device with CUDA events around K graph-replayed steps, max over ranks.
-``e2e`` = the same through the public Python API per call, with the query
-(and the appended token) copied from pinned host memory and the output copied
-back inside the timed region.  ``--impl reference`` times the reference's own
+whose total size is at least twice the 126 MB L2, in rotation order, so every
+step's cache was last touched a full rotation earlier (as successive layers of
+a model).
+
+Timing (CUDA events on the launching stream, max over ranks):
+* ``value`` / ``ms_per_step``: exactly K steps (a CUDA graph of the K steps,
+  replayed once), after W eager warm-up steps;
+* ``sustained``: the same step replayed from a graph of whole rotations until
+  at least one second of GPU time has been timed; the roofline's kernel time
+  is this figure when a step is one launch of the dominant kernel (it is, for
+  every workload at B=32);
+* ``e2e``: the same metric through the public host-buffer API, with the
+  query (and the appended token) copied from pinned host memory and the
+  output copied back inside the timed region;
+* ``verified``: outside the timed regions, one step's output is compared with
+  the CPU oracle (oracle/attention.py) on the same cache state.
+``sparse`` and ``dense`` sub-objects (informational) carry the same figures
+for the other two workloads.  ``--impl reference`` times the reference's own
 CPU PyTorch path (the restatement under oracle/) on the host cores instead.
 Multi-GPU: one process per GPU (torchrun), each rank decodes its own batch
 shard (weak scaling), no collective inside the timed region.
@@ -44,11 +56,18 @@ sys.path.insert(0, ROOT)
 B_PER_GPU = 32
 H, HKV, D, S, R, G = 64, 8, 128, 4, 128, 32
 L2_BYTES = 126 * 1024 * 1024
+SUSTAIN_S = 1.0  # GPU time of each sustained measurement
 METRIC = "decode-attn µs/step, tokens/s & HBM TB/s vs peak, W×L sweep, 1/2/4/8 GPU"
 WORKLOADS = {
-    "kivi": {"window": 256, "seq_len": 163_840, "config": "KIVI 2-bit sink+window decode + quantize-on-append"},
-    "sparse": {"window": 256, "seq_len": 163_840, "config": "fp16 sink+window ring-cache decode"},
-    "dense": {"window": None, "seq_len": 8_192, "config": "dense fp16 causal GQA decode"},
+    "kivi": {"window": 256, "seq_len": 163_840, "config": "KIVI 2-bit sink+window decode + quantize-on-append",
+             "tol": 1e-2},
+    "sparse": {"window": 256, "seq_len": 163_840, "config": "fp16 sink+window ring-cache decode", "tol": 2e-3},
+    "dense": {"window": None, "seq_len": 8_192, "config": "dense fp16 causal GQA decode", "tol": 2e-3},
+}
+KERNEL = {
+    "kivi": "kivi_stream_step_kernel (quantize-on-append + attention, one launch)",
+    "sparse": "window_decode_kernel (one CTA per unit)",
+    "dense": "fp16_decode_kernel (persistent, whole units)",
 }
 
 
@@ -183,12 +202,37 @@ class Workload:
         return o
 
     def attention_only(self, i: int):
-        """The dominant kernel alone (for the roofline): the attention launch
-        (for kivi with a one-launch step, that launch: append + attention)."""
+        """The attention launch of a two-launch KIVI step (append + attend)."""
         j = i % self.n_layers
-        if self.name == "kivi" and self.launches_per_step != 1:
-            return self.layers[j].attend(self.q[j])
-        return self.step(i)
+        return self.layers[j].attend(self.q[j])
+
+    def verify(self, rows: int = 2) -> dict:
+        """One step of layer 0, outside any timed region, against the CPU oracle
+        on the same cache state; returns {"max_abs_err", "tol", "ok"}."""
+        from oracle import attention as oa
+
+        tol = WORKLOADS[self.name]["tol"]
+        o = self.step(0)
+        torch.cuda.synchronize(self.device)
+        q = self.q[0]
+        if self.name == "kivi":
+            from oracle import kivi as ok
+
+            cache = self.layers[0]
+            st = {k: (v.detach().cpu().numpy() if hasattr(v, "detach") else v) for k, v in cache.state().items()}
+            ref = oa.stream_attention(q, st, cache.seq_len, ok.StreamGeometry(window=self.window))
+            got = o.float().cpu()
+        elif self.name == "sparse":
+            k, v = self.layers[0]
+            ref = oa.sparse_attention_slots(q.cpu().float(), k.cpu().float(), v.cpu().float(), self.seq_len,
+                                            self.window, S, ring_head=(self.seq_len - S) % self.window)
+            got = o.float().cpu()
+        else:  # the first `rows` sequences (the fp32 CPU oracle over all 32 x 8192 tokens is slow)
+            k, v = self.layers[0]
+            ref = oa.dense_attention(q[:rows].cpu().float(), k[:rows].cpu().float(), v[:rows].cpu().float())
+            got = o[:rows].float().cpu()
+        err = (got - ref).abs().max().item()
+        return {"max_abs_err": err, "tol": tol, "ok": bool(err < tol)}
 
 
 def cpu_reference_step(name: str, batch: int, threads: int):
@@ -236,6 +280,81 @@ def cpu_baseline(name: str, budget_s: float = 10.0):
                       f"torch threads={threads}"}
 
 
+# ----------------------------------------------------------------- timing
+def capture(stream, fn, indices):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in indices:
+            fn(i)
+    return g
+
+
+def preroll(stream, fn, start: int, n: int):
+    """Eager steps over one rotation ending just before `start`, so that the
+    next timed step's cache was touched a full rotation (>= 2x L2) earlier."""
+    for i in range(start - n, start):
+        fn(i)
+    stream.synchronize()
+
+
+def time_replays(stream, seq) -> float:
+    """ms of GPU time for replaying the graphs in `seq` back to back."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream.synchronize()
+    e0.record(stream)
+    for g in seq:
+        g.replay()
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1)
+
+
+class Timer:
+    """Exactly-K and sustained timings of one step function over a rotation of
+    n layers (indices continue the rotation, so L2 never holds the next step's
+    cache).  `agree` maxes a host number over ranks, so that every rank takes
+    the same replay counts and barriers."""
+
+    def __init__(self, stream, fn, n: int, start: int, barrier, agree):
+        self.stream, self.fn, self.n, self.start = stream, fn, n, start
+        self.barrier, self.agree = barrier, agree
+
+    def exact(self, k: int) -> float:
+        """ms per step over exactly k steps."""
+        n, start = self.n, self.start
+        per = k if k <= 4096 else n * max(1, 4096 // n)
+        full, rem = divmod(k, per)
+        g_main = capture(self.stream, self.fn, range(start, start + per))
+        g_rem = capture(self.stream, self.fn, range(start, start + rem)) if rem else None
+        g_main.replay()  # warm the graph
+        if g_rem is not None:
+            g_rem.replay()
+        preroll(self.stream, self.fn, start, n)
+        self.barrier()
+        ms = time_replays(self.stream, [g_main] * full + ([g_rem] if g_rem is not None else []))
+        del g_main, g_rem
+        return ms / k
+
+    def sustained(self, seconds: float = SUSTAIN_S) -> tuple[float, int]:
+        """(ms per step, steps timed) over >= `seconds` of GPU time."""
+        n, start = self.n, self.start
+        per = n * max(1, 256 // n)
+        g = capture(self.stream, self.fn, range(start, start + per))
+        g.replay()  # warm the graph
+        preroll(self.stream, self.fn, start, n)
+        est = self.agree(time_replays(self.stream, [g]))  # one replay, to size the timed run
+        reps = max(2, int(seconds * 1e3 / max(est, 1e-3) * 1.05) + 1)
+        while True:
+            preroll(self.stream, self.fn, start, n)
+            self.barrier()
+            ms = time_replays(self.stream, [g] * reps)
+            if self.agree(0.0 if ms >= seconds * 1e3 else 1.0) == 0.0:
+                break
+            reps = int(self.agree(reps * seconds * 1e3 / max(ms, 1e-3) * 1.1)) + 1
+        del g
+        return ms / (reps * per), reps * per
+
+
 # ----------------------------------------------------------------- main
 _STDOUT_FD = None
 
@@ -259,6 +378,139 @@ def emit(obj) -> None:
     print(json.dumps(obj), flush=True)
 
 
+def roofline(name: str, kernel_ms: float, kernel: str) -> dict:
+    peak, peak_kind = peaks()
+    bytes_step = algorithmic_bytes(name, B_PER_GPU)
+    achieved = bytes_step / (kernel_ms * 1e-3) / 1e9
+    traffic, src = NCU_TRAFFIC[name]
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "traffic": traffic * B_PER_GPU // 32, "traffic_source": src + " (one ncu capture, cold L2)",
+            "kernel": kernel, "kernel_us": kernel_ms * 1e3, "algorithmic_bytes_per_launch": bytes_step,
+            "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
+            else "fallback 6.65 TB/s"}
+
+
+def measure(name: str, a, dev, stream, barrier, max_over_ranks, rank: int, headline: bool) -> tuple:
+    """Device timings, roofline and oracle check of one workload on this rank;
+    returns (result dict, Workload)."""
+    wl = Workload(name, B_PER_GPU, dev, seed=1234 + rank)
+    n = wl.n_layers
+    with torch.cuda.stream(stream):
+        for i in range(a.warmup):
+            wl.step(i)
+        stream.synchronize()
+        start = a.warmup + n
+        t = Timer(stream, wl.step, n, start, barrier, max_over_ranks)
+        step_ms = t.exact(a.steps) if headline else None
+        sus_ms, sus_steps = t.sustained()
+        kernel_ms = sus_ms
+        kernel = KERNEL[name]
+        if name == "kivi" and wl.launches_per_step != 1:  # the attention launch alone
+            ta = Timer(stream, wl.attention_only, n, start, barrier, max_over_ranks)
+            kernel_ms, _ = ta.sustained()
+            kernel = "kivi_stream_decode_kernel (attention; the append is a separate launch)"
+        layered_ms = None
+        if headline and name == "kivi" and wl.launches_per_step == 1:
+            # informational: all layers' steps in one launch per rotation (decode_step_layers)
+            kv = importlib.import_module("numerics-and-sparse-attn_b200.kivi")
+            tl = Timer(stream, lambda i: kv.decode_step_layers(wl.layers, wl.q, wl.new_k, wl.new_v), 1, 1, barrier,
+                       max_over_ranks)
+            lay_ms, _ = tl.sustained(seconds=0.5)
+            layered_ms = lay_ms / n
+    if step_ms is not None:
+        step_ms = max_over_ranks(step_ms)
+    sus_ms = max_over_ranks(sus_ms)
+    kernel_ms = max_over_ranks(kernel_ms)
+    if layered_ms is not None:
+        layered_ms = max_over_ranks(layered_ms)
+    with torch.cuda.stream(stream):
+        check = wl.verify()
+    derr = wl.pkg.device_error(dev)
+    res = {"step_ms": step_ms, "sustained_ms": sus_ms, "sustained_steps": sus_steps, "kernel_ms": kernel_ms,
+           "kernel": kernel, "layered_ms": layered_ms, "check": check, "device_error": derr,
+           "l2": "per-step layer rotation over %d caches, %.0f MB total > 126 MB L2"
+                 % (n, n * algorithmic_bytes(name, B_PER_GPU) / 1e6)}
+    return res, wl
+
+
+def e2e_measure(name: str, wl: Workload, a, dev, stream, barrier, max_over_ranks) -> dict:
+    """Public host-buffer API per step (inputs from pinned host memory, output
+    back to pinned host memory, copies inside the timed region), and the
+    pure copy rates of the same bytes for reference."""
+    parts = [wl.q] + ([wl.new_k, wl.new_v] if name == "kivi" else [])
+    x_h = [torch.cat([p_[j].flatten() for p_ in parts]).cpu().pin_memory() for j in range(wl.n_layers)]
+    x_d = torch.empty_like(x_h[0], device=dev)
+    views, off = [], 0
+    for p_ in parts:
+        views.append(x_d[off:off + p_[0].numel()].view(p_[0].shape))
+        off += p_[0].numel()
+    o_d = torch.empty_like(wl.q[0])
+    o_h = [torch.empty_like(o_d, device="cpu").pin_memory() for _ in range(2)]
+    q_h = [x[:wl.q[0].numel()].view(wl.q[0].shape) for x in x_h]
+    h2d = x_h[0].numel() * 2
+    d2h = o_h[0].numel() * 2
+    steps = min(max(a.steps, 50), 400)
+    pipe = wl.pkg.HostPipe(h2d, d2h, device=dev, depth=2)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def host_call(i):
+        j = i % wl.n_layers
+        if name == "kivi":
+            wl.layers[j].decode_step_host(pipe, x_h[j], o_h[i % 2])
+        elif name == "sparse":
+            k, v = wl.layers[j]
+            wl.pkg.sparse_decode_attention_host(pipe, q_h[j], o_h[i % 2], k, v, wl.seq_len, wl.window,
+                                                ring_head=wl.ring_head)
+        else:
+            k, v = wl.layers[j]
+            wl.pkg.dense_decode_attention_host(pipe, q_h[j], o_h[i % 2], k, v, wl.seq_len)
+
+    def serial_call(i):
+        j = i % wl.n_layers
+        x_d.copy_(x_h[j], non_blocking=True)
+        if name == "kivi":
+            wl.out[j] = wl.layers[j].decode_step(views[0], views[1], views[2], out=o_d)
+            o = wl.out[j]
+        else:
+            o = wl.step(i, views[0])
+        o_h[0].copy_(o, non_blocking=True)
+
+    def timed(call, piped):
+        barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        if piped:
+            pipe.begin()
+        for i in range(steps):
+            call(i)
+        if piped:
+            pipe.end()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1) / steps)
+
+    def copy_rate(dst, srcs):
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(steps):
+            dst.copy_(srcs[i % len(srcs)], non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    with torch.cuda.stream(stream):
+        for i in range(4):  # warm the pipe's slots
+            host_call(i)
+        torch.cuda.synchronize()
+        serial_ms = timed(serial_call, False)
+        e2e_ms = timed(host_call, True)
+        pipe.close()
+        h2d_ms = max_over_ranks(copy_rate(x_d, x_h))
+        d2h_ms = max_over_ranks(copy_rate(o_h[0], [o_d]))
+    return {"ms": e2e_ms, "serial_ms": serial_ms, "h2d": h2d, "d2h": d2h, "h2d_ms": h2d_ms, "d2h_ms": d2h_ms,
+            "steps": steps}
+
+
 def main():
     quiet_stdout()
     ap = argparse.ArgumentParser()
@@ -268,16 +520,18 @@ def main():
     ap.add_argument("--workload", default=os.environ.get("NSA_BENCH_WORKLOAD", "kivi"), choices=list(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--headline-only", action="store_true", help="skip the other workloads' sub-objects")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
+    a.steps = max(1, a.steps)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     name = a.workload
-    wl = WORKLOADS[name]
-    config = {"workload": f"{name}: {wl['config']}", "global_batch": B_PER_GPU * world, "batch_per_gpu": B_PER_GPU,
-              "heads": "64/8/128", "seq_len": wl["seq_len"], "window": wl["window"], "sink": S,
+    wcfg = WORKLOADS[name]
+    config = {"workload": f"{name}: {wcfg['config']}", "global_batch": B_PER_GPU * world, "batch_per_gpu": B_PER_GPU,
+              "heads": "64/8/128", "seq_len": wcfg["seq_len"], "window": wcfg["window"], "sink": S,
               "parallelism": f"batch shard x{world} (no collective in the step)"}
 
     if a.impl == "reference":
@@ -309,7 +563,6 @@ def main():
 
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    wlobj = Workload(name, B_PER_GPU, dev, seed=1234 + rank)
     stream = torch.cuda.Stream(device=dev)
 
     def barrier():
@@ -319,144 +572,26 @@ def main():
     def max_over_ranks(x: float) -> float:
         return importlib.import_module("numerics-and-sparse-attn_b200.shard").max_over_ranks(x, dev)
 
-    with torch.cuda.stream(stream):
-        for i in range(a.warmup):
-            wlobj.step(i)
-        torch.cuda.synchronize()
-        # capture one rotation of steps (and of attention-only launches) as graphs
-        n = wlobj.n_layers
-        reps = max(1, -(-a.steps // n))
-        g_step = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_step, stream=stream):
-            for i in range(n * min(reps, max(1, 64 // n))):
-                wlobj.step(i)
-        per_graph = n * min(reps, max(1, 64 // n))
-        g_attn = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_attn, stream=stream):
-            for i in range(per_graph):
-                wlobj.attention_only(i)
-        for _ in range(2):
-            g_step.replay()
-            g_attn.replay()
-        torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    extra = {}
+    with clocks:
+        head, wl = measure(name, a, dev, stream, barrier, max_over_ranks, rank, headline=True)
+        e2e = e2e_measure(name, wl, a, dev, stream, barrier, max_over_ranks)
+        if not a.headline_only:
+            for other in WORKLOADS:
+                if other != name:
+                    res, owl = measure(other, a, dev, stream, barrier, max_over_ranks, rank, headline=False)
+                    extra[other] = res
+                    del owl
+                    torch.cuda.empty_cache()
 
-        n_graphs = max(1, -(-a.steps // per_graph))
-        steps_timed = n_graphs * per_graph
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        clocks = ClockSampler(local)
-        barrier()
-        torch.cuda.synchronize()
-        with clocks:
-            time.sleep(0.3)
-            e0.record(stream)
-            for _ in range(n_graphs):
-                g_step.replay()
-            e1.record(stream)
-            torch.cuda.synchronize()
-            step_ms = e0.elapsed_time(e1) / steps_timed
-            # dominant kernel alone, same rotation
-            e0.record(stream)
-            for _ in range(n_graphs):
-                g_attn.replay()
-            e1.record(stream)
-            torch.cuda.synchronize()
-            attn_ms = e0.elapsed_time(e1) / steps_timed
-        # informational (kivi): all layers' steps in one launch per rotation
-        # (decode_step_layers), for decode loops that have every layer's query at once
-        layered_ms = None
-        if name == "kivi" and wlobj.launches_per_step == 1:
-            kv = importlib.import_module("numerics-and-sparse-attn_b200.kivi")
-            g_lay = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g_lay, stream=stream):
-                for _ in range(per_graph // n):
-                    kv.decode_step_layers(wlobj.layers, wlobj.q, wlobj.new_k, wlobj.new_v)
-            g_lay.replay()
-            torch.cuda.synchronize()
-            e0.record(stream)
-            for _ in range(n_graphs):
-                g_lay.replay()
-            e1.record(stream)
-            torch.cuda.synchronize()
-            layered_ms = e0.elapsed_time(e1) / steps_timed
-            del g_lay
-        barrier()
-        step_ms = max_over_ranks(step_ms)
-        attn_ms = max_over_ranks(attn_ms)
-        if layered_ms is not None:
-            layered_ms = max_over_ranks(layered_ms)
-
-        # e2e through the public API with HOST buffers: each step's inputs (q, and
-        # for kivi the new token's K and V) sit packed in a pinned host buffer and
-        # the output goes back to pinned host memory.  Headline: one host-buffer
-        # call per step (the *_host entry points: copy in, decode, copy out on a
-        # two-slot pipe, so one step's copies overlap the next step's decode).
-        # Also reported: the same through the device-tensor API with the copies
-        # issued around it on the compute stream (copy, decode, copy in sequence).
-        parts = [wlobj.q] + ([wlobj.new_k, wlobj.new_v] if name == "kivi" else [])
-        x_h = [torch.cat([p_[j].flatten() for p_ in parts]).cpu().pin_memory() for j in range(wlobj.n_layers)]
-        x_d = torch.empty_like(x_h[0], device=dev)
-        views, off = [], 0
-        for p_ in parts:
-            views.append(x_d[off:off + p_[0].numel()].view(p_[0].shape))
-            off += p_[0].numel()
-        o_d = torch.empty_like(wlobj.q[0])
-        o_h = [torch.empty_like(o_d, device="cpu").pin_memory() for _ in range(2)]
-        q_h = [x[:wlobj.q[0].numel()].view(wlobj.q[0].shape) for x in x_h]
-        h2d = x_h[0].numel() * 2
-        d2h = o_h[0].numel() * 2
-        e2e_steps = min(a.steps, 200)
-        pipe = wlobj.pkg.HostPipe(h2d, d2h, device=dev, depth=2)
-
-        def host_call(i):
-            j = i % wlobj.n_layers
-            if name == "kivi":
-                wlobj.layers[j].decode_step_host(pipe, x_h[j], o_h[i % 2])
-            elif name == "sparse":
-                k, v = wlobj.layers[j]
-                wlobj.pkg.sparse_decode_attention_host(pipe, q_h[j], o_h[i % 2], k, v, wlobj.seq_len, wlobj.window,
-                                                       ring_head=wlobj.ring_head)
-            else:
-                k, v = wlobj.layers[j]
-                wlobj.pkg.dense_decode_attention_host(pipe, q_h[j], o_h[i % 2], k, v, wlobj.seq_len)
-
-        def serial_call(i):
-            j = i % wlobj.n_layers
-            x_d.copy_(x_h[j], non_blocking=True)
-            if name == "kivi":
-                o = wlobj.layers[j].decode_step(views[0], views[1], views[2], out=o_d)
-                wlobj.out[j] = o
-            else:
-                o = wlobj.step(i, views[0])
-            o_h[0].copy_(o, non_blocking=True)
-
-        def timed(call, piped):
-            barrier()
-            torch.cuda.synchronize()
-            e0.record(stream)
-            if piped:
-                pipe.begin()
-            for i in range(e2e_steps):
-                call(i)
-            if piped:
-                pipe.end()
-            e1.record(stream)
-            torch.cuda.synchronize()
-            return max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
-
-        for i in range(4):  # warm the pipe's slots
-            host_call(i)
-        torch.cuda.synchronize()
-        e2e_serial_ms = timed(serial_call, False)
-        e2e_ms = timed(host_call, True)
-        pipe.close()
-        derr = wlobj.pkg.device_error(dev)
-
-    # verification outside the timed region: assemble all ranks' outputs with
-    # one all-gather (NCCL over NVLink) and check each rank's slice came back
-    verified = bool(torch.isfinite(wlobj.out[0].float()).all().item()) and derr == 0
+    # verification outside the timed regions: the oracle check of one step on
+    # this rank, and (N > 1) all ranks' outputs assembled with one all-gather
+    # (NCCL over NVLink) with each rank's slice checked
+    verified = head["check"]["ok"] and head["device_error"] == 0
     if world > 1:
         shard = importlib.import_module("numerics-and-sparse-attn_b200.shard")
-        mine = wlobj.out[0].contiguous()
+        mine = wl.out[0].contiguous()
         full = shard.gather_outputs(mine, B_PER_GPU * world, HKV)
         sh = shard.shard_units(B_PER_GPU * world, HKV, world, rank)
         verified = verified and bool(torch.isfinite(full.float()).all().item()) and \
@@ -465,15 +600,16 @@ def main():
         torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MIN)
         verified = flag.item() == 1.0
 
+    step_ms = head["step_ms"]
     bytes_step = algorithmic_bytes(name, B_PER_GPU)
-    peak, peak_kind = peaks()
-    achieved = bytes_step / (attn_ms * 1e-3) / 1e9
+    launches = wl.launches_per_step if name == "kivi" else 1
+    e2e_bound = max(e2e["h2d_ms"], e2e["d2h_ms"], head["sustained_ms"])
     line = {
         "metric": METRIC,
         "value": B_PER_GPU * world / (step_ms * 1e-3),
         "unit": "tokens/s",
         "n_gpus": world,
-        "steps": steps_timed,
+        "steps": a.steps,
         "warmup": a.warmup,
         "ms_per_step": step_ms,
         "us_per_step": step_ms * 1e3,
@@ -482,42 +618,47 @@ def main():
         "vs_baseline": None,
         "dtype": "fp16 (2-bit codes, fp32 accumulate)" if name == "kivi" else "fp16 (fp32 accumulate)",
         "data": "synthetic N(0,1) fp16, seeded; random caches, no checkpoint",
-        "config": dict(config, l2="per-step layer rotation over %d caches, %.0f MB total > 126 MB L2"
-                       % (wlobj.n_layers, wlobj.n_layers * bytes_step / 1e6)),
+        "config": config,
+        "l2": head["l2"],
         "hbm_tbs_step": bytes_step / (step_ms * 1e-3) / 1e12,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": (NCU_TRAFFIC[name][0] * B_PER_GPU // 32) if name in NCU_TRAFFIC else None,
-                     "traffic_source": (NCU_TRAFFIC[name][1] + " (one ncu capture, cold L2)")
-                     if name in NCU_TRAFFIC else None,
-                     "kernel": ("kivi_stream_step_kernel (quantize-on-append + attention, one launch)"
-                                if wlobj.launches_per_step == 1 else "kivi_stream_decode_kernel (attention)")
-                     if name == "kivi" else
-                     ("window_decode_kernel (one CTA per unit)" if name == "sparse" and
-                      B_PER_GPU * HKV >= torch.cuda.get_device_properties(dev).multi_processor_count and
-                      S + WORKLOADS[name]["window"] <= 384 else "fp16_decode_kernel (persistent)"),
-                     "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
-                     else "fallback 6.65 TB/s", "kernel_us": attn_ms * 1e3,
-                     "algorithmic_bytes_per_launch": bytes_step},
-        "e2e": {"value": B_PER_GPU * world / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+        "sustained": {"steps": head["sustained_steps"], "ms_per_step": head["sustained_ms"],
+                      "timed_s": head["sustained_steps"] * head["sustained_ms"] * 1e-3,
+                      "tokens_per_s": B_PER_GPU * world / (head["sustained_ms"] * 1e-3),
+                      "note": "the same step from a graph of whole layer rotations, replayed for >= 1 s of GPU time"},
+        "roofline": roofline(name, head["kernel_ms"], head["kernel"]),
+        "e2e": {"value": B_PER_GPU * world / (e2e["ms"] * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"], "ms_per_step": e2e["ms"],
+                "steps": e2e["steps"],
                 "path": "one public host-buffer call per step (decode_step_host / *_decode_attention_host: "
                         "H2D, decode, D2H on a two-slot pipe)",
-                "device_api_serial_ms_per_step": e2e_serial_ms},
-        "gpu_launches": steps_timed * wlobj.launches_per_step,
+                "h2d_gbs": e2e["h2d"] / (e2e["h2d_ms"] * 1e-3) / 1e9,
+                "d2h_gbs": e2e["d2h"] / (e2e["d2h_ms"] * 1e-3) / 1e9,
+                "bound_ms": e2e_bound, "ms_over_bound": e2e["ms"] / e2e_bound,
+                "device_api_serial_ms_per_step": e2e["serial_ms"]},
+        "gpu_launches": a.steps * launches,
         **({"layer_batched": {
-            "layers_per_launch": wlobj.n_layers, "us_per_layer_step": layered_ms * 1e3,
-            "tokens_per_s_per_layer": B_PER_GPU * world / (layered_ms * 1e-3),
-            "hbm_tbs": algorithmic_bytes(name, B_PER_GPU) / (layered_ms * 1e-3) / 1e12,
+            "layers_per_launch": wl.n_layers, "us_per_layer_step": head["layered_ms"] * 1e3,
+            "tokens_per_s_per_layer": B_PER_GPU * world / (head["layered_ms"] * 1e-3),
+            "hbm_tbs": bytes_step / (head["layered_ms"] * 1e-3) / 1e12,
+            "frac": bytes_step / (head["layered_ms"] * 1e-3) / 1e9 / peaks()[0],
             "note": "informational: every layer's decode step (same inputs as the headline) in one launch "
-                    "(decode_step_layers); needs all layers' queries at once"}} if layered_ms is not None else {}),
+                    "(decode_step_layers); needs all layers' queries at once"}} if head["layered_ms"] else {}),
         "clocks": clocks.summary(),
         "verified": verified,
+        "oracle_check": head["check"],
     }
+    for other, res in extra.items():
+        line[other] = {"config": WORKLOADS[other]["config"], "seq_len": WORKLOADS[other]["seq_len"],
+                       "window": WORKLOADS[other]["window"], "us_per_step": res["sustained_ms"] * 1e3,
+                       "tokens_per_s": B_PER_GPU * world / (res["sustained_ms"] * 1e-3),
+                       "sustained_steps": res["sustained_steps"], "l2": res["l2"],
+                       "roofline": roofline(other, res["kernel_ms"], res["kernel"]),
+                       "verified": res["check"]["ok"] and res["device_error"] == 0, "oracle_check": res["check"],
+                       "note": "informational (not the headline workload)"}
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(name)
     if world > 1:
         torch.distributed.barrier()
-        del g_step, g_attn
         torch.distributed.destroy_process_group()
     if rank == 0:
         emit(line)

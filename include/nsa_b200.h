@@ -133,10 +133,14 @@ int nsa_ring_decode_step(const void* q, void* k_cache, void* v_cache, void* o,
  * runtime that reserves all device memory through its own pool, or a plain C
  * caller without a device allocator.  The split-K scratch lives in a static
  * 4 MiB device array inside this library (held by every GPU that loads it
- * until exit); shapes whose scratch does not fit are rejected with
- * NSA_ERR_UNSUPPORTED.  The first call on a device looks the array up and
- * clears it -- make that call before any stream capture.  All calls on a
- * device share the array: calls that overlap on the GPU race on it. */
+ * until exit).  Only launches that split a unit over several CTAs use it
+ * (fewer units than SMs, or windows long enough for stream-K); those whose
+ * scratch does not fit are rejected with NSA_ERR_UNSUPPORTED, while shapes
+ * that keep every unit whole (one unit per CTA) have no size limit.  The
+ * first call on a device that needs the array looks it up and clears it --
+ * make that call before any stream capture.  An empty batch returns 0
+ * without any CUDA call.  All calls on a device share the array: calls that
+ * overlap on the GPU race on it. */
 int nsa_sparse_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, void* o,
                               int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
                               int64_t window, int64_t sink, int64_t seq_len,

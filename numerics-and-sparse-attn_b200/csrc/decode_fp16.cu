@@ -631,22 +631,37 @@ int check_common(const void* q, const void* k, const void* v, const void* o, int
   return NSA_OK;
 }
 
+// Whether a launch of plan s over `cap` slots touches the split-K scratch
+// (tickets and partials): only the persistent kernel with some unit split
+// over several CTAs does; the window kernel and whole-unit plans store every
+// output directly.
+bool uses_scratch(const Params& p, const Split& s, int64_t cap) {
+  if (p.mode == kSparse && use_window_kernel(s.n_units, cap)) return false;
+  return s.max_pieces > 1;
+}
+
 int launch(Params& p, const Split& s, const void* k, const void* v, int64_t cap, void* ws, size_t ws_bytes,
            cudaStream_t stream) {
   if (s.n_units == 0) return NSA_OK;
   if (p.mode == kSparse && use_window_kernel(s.n_units, cap)) return launch_window(p, s.n_units, k, v, cap, stream);
   if (cap > (int64_t(1) << 31) - kTile) return fail(NSA_ERR_UNSUPPORTED, "cache length too large for TMA coordinates");
-  const size_t need = workspace_bytes(s);
-  if (!ws || ws_bytes < need)
-    return fail(NSA_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, ws ? ws_bytes : size_t(0));
-  if (!aligned16(ws)) return fail(NSA_ERR_ALIGN, "workspace must be 16-byte aligned");
-  uint8_t* w = static_cast<uint8_t*>(ws);
-  const size_t counters = ((s.n_units * sizeof(int)) + 255) & ~size_t(255);
-  const size_t pieces = static_cast<size_t>(s.n_units) * s.max_pieces;
-  const size_t lse = ((pieces * kGroupHeads * sizeof(float)) + 255) & ~size_t(255);
-  p.counters = reinterpret_cast<int*>(w);
-  p.part_lse = reinterpret_cast<float*>(w + counters);
-  p.part_o = reinterpret_cast<float*>(w + counters + lse);
+  if (uses_scratch(p, s, cap)) {
+    const size_t need = workspace_bytes(s);
+    if (!ws || ws_bytes < need)
+      return fail(NSA_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, ws ? ws_bytes : size_t(0));
+    if (!aligned16(ws)) return fail(NSA_ERR_ALIGN, "workspace must be 16-byte aligned");
+    uint8_t* w = static_cast<uint8_t*>(ws);
+    const size_t counters = ((s.n_units * sizeof(int)) + 255) & ~size_t(255);
+    const size_t pieces = static_cast<size_t>(s.n_units) * s.max_pieces;
+    const size_t lse = ((pieces * kGroupHeads * sizeof(float)) + 255) & ~size_t(255);
+    p.counters = reinterpret_cast<int*>(w);
+    p.part_lse = reinterpret_cast<float*>(w + counters);
+    p.part_o = reinterpret_cast<float*>(w + counters + lse);
+  } else {  // whole units: every piece stores its output directly
+    p.counters = nullptr;
+    p.part_lse = nullptr;
+    p.part_o = nullptr;
+  }
   p.n_units = s.n_units;
   p.tiles_per_unit = s.tiles_per_unit;
   p.total_tiles = s.total_tiles;
@@ -825,11 +840,15 @@ int nsa_ring_decode_step(const void* q, void* k_cache, void* v_cache, void* o, i
 //
 // Facts a caller must know:
 // * The array is kNoAllocScratchBytes (4 MiB) per GPU, held by every GPU that
-//   loads this library until the process exits.  Shapes whose scratch does not
-//   fit are rejected with NSA_ERR_UNSUPPORTED before anything is launched.
-// * The first call on a device looks up the array's device address
-//   (cudaGetSymbolAddress) and clears it (cudaMemset); make that first call
-//   before any stream capture.  Later calls on the device do neither.
+//   loads this library until the process exits.  Only plans that split a unit
+//   over several CTAs use it; among those, shapes whose scratch does not fit
+//   are rejected with NSA_ERR_UNSUPPORTED before anything is launched.  Plans
+//   that keep units whole (the window kernel, whole-unit persistent plans)
+//   never touch it and have no size limit.
+// * The first call on a device that uses the array looks up its device
+//   address (cudaGetSymbolAddress) and clears it (cudaMemset); make that first
+//   call before any stream capture.  Later calls on the device do neither, and
+//   an empty batch returns before any CUDA call.
 // * Every call on a device shares the one array.  The kernel leaves the parts
 //   it used zeroed again, but calls that overlap on the GPU (different streams
 //   without ordering) race on it and may return wrong results.  After a call
@@ -888,15 +907,8 @@ int nsa_sparse_decode_noalloc(const void* q, const void* k_cache, const void* v_
   if (window < 0 || sink < 0 || window + sink < 1 || window + sink > (int64_t(1) << 30))
     return fail(NSA_ERR_INVALID, "need window, sink >= 0 and 1 <= window + sink <= 2^30");
   if (seq_len < 0) return fail(NSA_ERR_INVALID, "seq_len must be >= 0");
+  if (batch * n_kv_heads == 0) return NSA_OK;  // nothing to do: no set-up, no CUDA call
   const Split s = plan(batch * n_kv_heads, window + sink);
-  const size_t need = workspace_bytes(s);
-  if (need > kNoAllocScratchBytes)
-    return fail(NSA_ERR_UNSUPPORTED,
-                "this shape needs %zu bytes of split-K scratch; the allocation-free entry point has %zu "
-                "(use nsa_sparse_decode with a workspace)",
-                need, kNoAllocScratchBytes);
-  void* scratch = noalloc_scratch();
-  if (!scratch) return NSA_ERR_CUDA;
   Params p{};
   p.q = static_cast<const __half*>(q);
   p.o = static_cast<__half*>(o);
@@ -908,6 +920,17 @@ int nsa_sparse_decode_noalloc(const void* q, const void* k_cache, const void* v_
   p.window = static_cast<int>(window);
   p.sink = static_cast<int>(sink);
   p.scale_log2 = sm_scale * 1.4426950408889634f;
+  // Only plans that split a unit over several CTAs use scratch; the others
+  // (the window kernel, whole units) need neither the array nor its size limit.
+  if (!uses_scratch(p, s, window + sink)) return launch(p, s, k_cache, v_cache, window + sink, nullptr, 0, stream);
+  const size_t need = workspace_bytes(s);
+  if (need > kNoAllocScratchBytes)
+    return fail(NSA_ERR_UNSUPPORTED,
+                "this shape needs %zu bytes of split-K scratch; the allocation-free entry point has %zu "
+                "(use nsa_sparse_decode with a workspace)",
+                need, kNoAllocScratchBytes);
+  void* scratch = noalloc_scratch();
+  if (!scratch) return NSA_ERR_CUDA;
   return launch(p, s, k_cache, v_cache, window + sink, scratch, kNoAllocScratchBytes, stream);
 }
 

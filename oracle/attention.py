@@ -5,16 +5,16 @@ reference's, they follow the device of their inputs (CPU in the CPU suite; the
 GPU parity tests may run them on CUDA tensors as the fp32 checker).
 
 * ``dense_attention``          test_dense_correctness.py:13-30
-* ``sparse_attention_full``    test_sparse_correctness.py:84-110, with the GQA
+* ``sparse_attention_full``    test_sparse_correctness.py:22-48, with the GQA
                                group derived from the shapes instead of the
                                module constant GQA_GROUP (the reference's
                                version raises on 8 query / 2 KV heads).
-* ``build_compacted_cache``    test_sparse_correctness.py:113-134, shape-generic.
+* ``build_compacted_cache``    test_sparse_correctness.py:51-72, shape-generic.
 * ``slot_validity``            sparse_kernel.py:15-46 (``_kv_indices``) plus the
                                ring-buffer head offset used by the ring layout.
 * ``sparse_attention_slots``   what sparse_kernel.py:67-102 computes: softmax
                                over the valid physical slots of a cache.
-* ``quantized_attention``      test_quantized_attention_correctness.py:288-317.
+* ``quantized_attention``      test_quantized_attention_correctness.py:32-61.
 """
 from __future__ import annotations
 
@@ -23,7 +23,7 @@ import torch
 
 from . import kivi as _kivi
 
-GARBAGE_VALUE = 1e4  # test_sparse_correctness.py:77
+GARBAGE_VALUE = 1e4  # test_sparse_correctness.py:15
 
 
 def _attend(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float,
@@ -52,7 +52,7 @@ def dense_attention(q, k, v, sm_scale=None):
 
 def sparse_attention_full(q, k_full, v_full, seq_len: int, window: int, sink: int, sm_scale=None):
     """StreamingLLM mask over the full un-evicted context
-    (test_sparse_correctness.py:84-110): dense until seq_len > sink+window,
+    (test_sparse_correctness.py:22-48): dense until seq_len > sink+window,
     then ``pos < sink | pos >= seq_len - window``."""
     if sm_scale is None:
         sm_scale = q.shape[-1] ** -0.5
@@ -66,7 +66,7 @@ def sparse_attention_full(q, k_full, v_full, seq_len: int, window: int, sink: in
 
 def build_compacted_cache(k_full, v_full, seq_len: int, window: int, sink: int,
                           garbage: float = GARBAGE_VALUE):
-    """[B, KV, sink+window, D] compacted cache (test_sparse_correctness.py:113-134):
+    """[B, KV, sink+window, D] compacted cache (test_sparse_correctness.py:51-72):
     slot i < sink holds position i; slot sink+i holds position
     seq_len-window+i; slots whose position does not exist hold ``garbage``."""
     b, kv, _, d = k_full.shape
@@ -131,7 +131,7 @@ def sparse_attention_slots(q, k_cache, v_cache, seq_len: int, window: int, sink:
 
 
 def quantized_attention(q, win_old_len: int, cache: dict, sink: int = 4, sm_scale=None):
-    """KIVI oracle (test_quantized_attention_correctness.py:288-317): dequantize
+    """KIVI oracle (test_quantized_attention_correctness.py:32-61): dequantize
     sink[:sink] + window-old + residual from the same packed tensors and run
     fp32 attention over their concatenation."""
     d = q.shape[-1]

@@ -118,7 +118,7 @@ def main(ref_dir):
     w.case("quant_sink_pad", {"op": "sink_pad", "seed": 2, "input_sha256": gi.sha(sink)},
            {"k_packed": p, "k_scale": s, "k_zero": z, "v_packed": pv, "v_scale": sv, "v_zero": zv})
 
-    # ---- isolated dequant tiles (test_dequantize_tile_isolated.py:197-251) --
+    # ---- isolated dequant tiles (test_dequantize_tile_isolated.py:66-120) --
     print("dequant tiles", flush=True)
     for name, seed, fn in (("dequant_k_tile", 4, "k"), ("dequant_v_tile", 5, "v")):
         x = gi.randn((1, 1, 256, 128), seed)

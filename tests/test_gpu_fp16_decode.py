@@ -98,7 +98,7 @@ def test_sparse_matches_reference_golden(name):
 @pytest.mark.parametrize("L,W", [(2, 256), (100, 256), (5000, 256), (2, 0), (10_000, 0), (163_840, 256),
                                  (261, 256), (300, 32), (4100, 4096), (20_000, 1024)])
 def test_sparse_reference_cases_full_batch(L, W):
-    """test_sparse_correctness.py:137-173 cases at B=32 plus wrap-around."""
+    """test_sparse_correctness.py:83-89 cases at B=32 plus wrap-around."""
     B = 32
     g = torch.Generator(device=DEV).manual_seed(L * 7 + W)
     q = torch.randn(B, 64, 128, device=DEV, generator=g).half()
@@ -108,7 +108,7 @@ def test_sparse_reference_cases_full_batch(L, W):
     kv_pos = torch.randn(B, 8, len(pos), 128, device=DEV, generator=g).half()
     vv_pos = torch.randn(B, 8, len(pos), 128, device=DEV, generator=g).half()
     # compacted and ring caches; every slot not holding an attended position
-    # keeps GARBAGE_VALUE (test_sparse_correctness.py:77)
+    # keeps GARBAGE_VALUE (test_sparse_correctness.py:15)
     kc = torch.full((B, 8, S + W, 128), oa.GARBAGE_VALUE, device=DEV).half()
     vc = kc.clone()
     kr, vr = kc.clone(), kc.clone()

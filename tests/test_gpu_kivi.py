@@ -86,7 +86,7 @@ def test_quantize_sink_padding():
 
 @pytest.mark.parametrize("name,axis", [("dequant_k_tile", 2), ("dequant_v_tile", 3)])
 def test_host_dequant_matches_reference_tile(name, axis):
-    """test_dequantize_tile_isolated.py:197-251 through the host-callable form."""
+    """test_dequantize_tile_isolated.py:66-120 through the host-callable form."""
     meta, arrays = fixtures.load(name)
     x = gi.randn((1, 1, 256, 128), meta["seed"]).to(DEV)
     if axis == 2:

@@ -106,7 +106,7 @@ def test_sparse_oracle_matches_reference_kernel(name):
     # the compacted-cache builder restatement reproduces the reference's bytes
     assert gi.sha(torch.cat([kc.half().reshape(-1), vc.half().reshape(-1)])) == meta["cache_sha256"]
     ref = torch.from_numpy(arrays["o"]).float()
-    # the masked full-context oracle (test_sparse_correctness.py:84-110) on the
+    # the masked full-context oracle (test_sparse_correctness.py:22-48) on the
     # fp16-rounded inputs the kernel saw
     o_full = oa.sparse_attention_full(q.half().float(), kf.half().float(), vf.half().float(), L, W, 4)
     assert (o_full - ref).abs().max().item() < 2e-3
