@@ -39,7 +39,7 @@ import torch.distributed as dist
 from constants import (BATCH, CONTEXT_LENGTHS, D_HEAD, N_HEADS, N_KV_HEADS, RESIDUAL_SIZE, SINK_SIZE,
                        WINDOW_SIZES)
 from dense_kernel import dense_decode_attention
-from quant_kernel import build_quantized_kv_cache, sparse_decode_attention_quantized
+from quant_kernel import KiviCache, build_quantized_kv_cache, sparse_decode_attention_quantized
 from sparse_kernel import sparse_decode_attention
 
 B_FIXED_FP16 = 1_048_576  # Q + O bytes (benchmark.py:30 of the reference)
@@ -187,9 +187,20 @@ def benchmark(lengths, windows, timer, peak, batch, gtimer=None):
     return results
 
 
+def stream_bytes(batch: int, window: int) -> int:
+    """Attended bytes of a streaming KIVI cache with window < RESIDUAL_SIZE
+    (every window token still in the fp16 residual): per (batch, kv head) the
+    padded sink group's 3 KiB record plus W fp16 K and V rows, plus q and o."""
+    units = batch * N_KV_HEADS
+    return units * (3 * 1024 + window * 2 * D_HEAD * 2) + 2 * batch * N_HEADS * D_HEAD * 2
+
+
 def benchmark_quantized(lengths, windows, timer, peak, batch, gtimer=None):
     """Quantized sparse vs native sparse vs dense (the reference's
-    benchmark_quantized()); W < RESIDUAL_SIZE is skipped as there."""
+    benchmark_quantized()).  The reference skips W < RESIDUAL_SIZE
+    (its benchmark.py:86; build_quantized_kv_cache needs W >= R); here those
+    windows are timed through the streaming cache (KiviCache: the sink group
+    quantized, the window still in the fp16 residual), marked layout=stream."""
     sm_scale = D_HEAD ** -0.5
     gen = torch.Generator(device="cuda").manual_seed(1 + RANK)
     keys = ["k_residual", "v_residual", "k_sink_packed", "k_sink_scale", "k_sink_zero", "v_sink_packed",
@@ -201,20 +212,34 @@ def benchmark_quantized(lengths, windows, timer, peak, batch, gtimer=None):
         k_dense = randn(batch, N_KV_HEADS, L, D_HEAD, gen=gen)
         v_dense = randn(batch, N_KV_HEADS, L, D_HEAD, gen=gen)
         ms_dense = timer(lambda: dense_decode_attention(q, k_dense, v_dense, seq_len=L, sm_scale=sm_scale))
-        for W in [w for w in windows if w >= RESIDUAL_SIZE]:
+        for W in [w for w in windows if w > 0]:
             kc = randn(batch, N_KV_HEADS, SINK_SIZE + W, D_HEAD, gen=gen)
             vc = randn(batch, N_KV_HEADS, SINK_SIZE + W, D_HEAD, gen=gen)
             ms_sparse = timer(lambda: sparse_decode_attention(q, kc, vc, seq_len=L, window=W))
-            cache = build_quantized_kv_cache(kc, vc)  # setup, not timed
-            args = [cache[k] for k in keys]
-            ms_quant = timer(lambda: sparse_decode_attention_quantized(q, *args, seq_len=L, window=W))
             gms_quant = None
-            bytes_quant = (sum(t.numel() * t.element_size() for t in args) + 2 * q.numel() * q.element_size()) * WORLD
-            if gtimer:
-                copies = [args] + [[t.clone() for t in args] for _ in range(n_copies(bytes_quant // WORLD) - 1)]
-                gms_quant = gtimer([lambda a_=a_: sparse_decode_attention_quantized(q, *a_, seq_len=L, window=W)
-                                    for a_ in copies])
-                del copies
+            if W >= RESIDUAL_SIZE:
+                layout = "reference"
+                cache = build_quantized_kv_cache(kc, vc)  # setup, not timed
+                args = [cache[k] for k in keys]
+                ms_quant = timer(lambda: sparse_decode_attention_quantized(q, *args, seq_len=L, window=W))
+                bytes_quant = (sum(t.numel() * t.element_size() for t in args)
+                               + 2 * q.numel() * q.element_size()) * WORLD
+                if gtimer:
+                    copies = [args] + [[t.clone() for t in args] for _ in range(n_copies(bytes_quant // WORLD) - 1)]
+                    gms_quant = gtimer([lambda a_=a_: sparse_decode_attention_quantized(q, *a_, seq_len=L, window=W)
+                                        for a_ in copies])
+                    del copies
+            else:  # the streaming cache after L appends (setup, not timed); attention only
+                layout = "stream"
+                cache = KiviCache.synthetic(batch, N_KV_HEADS, W, L, generator=gen)
+                args = []
+                ms_quant = timer(lambda: cache.attend(q))
+                bytes_quant = stream_bytes(batch, W) * WORLD
+                if gtimer:
+                    copies = [cache] + [KiviCache.synthetic(batch, N_KV_HEADS, W, L, generator=gen)
+                                        for _ in range(n_copies(bytes_quant // WORLD) - 1)]
+                    gms_quant = gtimer([lambda c_=c_: c_.attend(q) for c_ in copies])
+                    del copies
             bytes_sparse = int((B_FIXED_FP16 + C_FP16 * (W + SINK_SIZE)) * batch * WORLD / BATCH)
             predicted = bytes_sparse / bytes_quant
             measured = ms_sparse / ms_quant
@@ -225,7 +250,7 @@ def benchmark_quantized(lengths, windows, timer, peak, batch, gtimer=None):
                 "predicted_marginal_multiplier": predicted, "measured_marginal_multiplier": measured,
                 "gap_pct": 100 * (measured - predicted) / predicted,
                 "tbs_quantized": tbs_quant, "frac_quantized": tbs_quant / (peak * WORLD),
-                "n_gpus": WORLD, "batch": batch * WORLD,
+                "n_gpus": WORLD, "batch": batch * WORLD, "layout": layout,
                 **({"ms_quantized_graph": gms_quant, "tbs_quantized_graph": bytes_quant / gms_quant / 1e9}
                    if gtimer else {}),
             })

@@ -212,7 +212,7 @@ struct WarpAttn {
 // 132 floats so the fragment scatter is conflict-free.
 constexpr int kRedStride = 132;
 constexpr int kXferWords = 36;  // 32 accumulators + 2 maxima + 2 partial sums
-struct EpilogueSmem {
+struct alignas(16) EpilogueSmem {  // 16-byte aligned: merge_warps reads float4s
   union {
     float xfer[kGroupWarps][kXferWords][32];
     struct {
@@ -292,12 +292,23 @@ __device__ __forceinline__ void merge_warps(const EpilogueSmem& ep, int head, in
     f[w] = (mw == -INFINITY) ? 0.f : fast_exp2(mw - mstar);
     L += f[w] * ep.red.l[w][head];
   }
+  static_assert(N % 4 == 0, "float4 reads of the published rows");
 #pragma unroll
-  for (int i = 0; i < N; ++i) {
-    float a = 0.f;
+  for (int i = 0; i < N; i += 4) {
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int w = 0; w < kGroupWarps; ++w) a += f[w] * ep.red.o[w][head][d0 + i];
-    o[i] = __fdividef(a, L);  // L == 0 (nothing attended): 0/0 = NaN, as the reference
+    for (int w = 0; w < kGroupWarps; ++w) {  // rows are 528 bytes apart and d0 % 4 == 0: 16-byte aligned
+      const float4 v = *reinterpret_cast<const float4*>(&ep.red.o[w][head][d0 + i]);
+      a.x += f[w] * v.x;
+      a.y += f[w] * v.y;
+      a.z += f[w] * v.z;
+      a.w += f[w] * v.w;
+    }
+    // L == 0 (nothing attended): 0/0 = NaN, as the reference
+    o[i] = __fdividef(a.x, L);
+    o[i + 1] = __fdividef(a.y, L);
+    o[i + 2] = __fdividef(a.z, L);
+    o[i + 3] = __fdividef(a.w, L);
   }
   lse = (L > 0.f) ? mstar + __log2f(L) : -INFINITY;
 }

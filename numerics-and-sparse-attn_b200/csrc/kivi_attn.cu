@@ -129,7 +129,6 @@ static_assert(offsetof(Smem, f) == 0 && kFStageBytes % 1024 == 0 && kFRegion % 1
 static_assert(offsetof(Smem, qb) % 16 == 0 && kQStageBytes % 16 == 0, "bulk-copy destinations");
 static_assert(offsetof(Smem, qpad) % 16 == 0 && (kQPadStride * 2) % 16 == 0, "16-byte stores");
 static_assert(sizeof(EpilogueSmem) <= sizeof(uint8_t[kFStages][kFStageBytes]), "epilogue alias");
-static_assert(kFStages < kCWarps, "warps 1..kFStages issue the first F-tiles");
 // The dynamic shared-memory window of a CTA starts 1024-byte aligned on sm_100
 // (the kernel checks it); 1 KiB per CTA is reserved by the system.
 constexpr size_t kSmemBytes = sizeof(Smem);
@@ -877,7 +876,8 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   // streaming layout: the free stages' F-tiles, one warp each: their copies are issued while
   // lane 0 of warp 0 issues batch 0 (each copy request takes hundreds of cycles to issue):
   // -0.1 to -0.2 us.  (The reference layout's tile loads need the tensor maps lane 0 prefetches.)
-  if (kRec && lane == 0 && warp >= 1 && warp <= kFStages) iss.first_f(warp - 1);
+  if (kRec && lane == 0 && warp >= 1)
+    for (int i = warp - 1; i < kFStages; i += kCWarps - 1) iss.first_f(i);
   int len = static_cast<int>(len64);
   if (kRec && (len64 < 0 || len64 >= kMaxUnitLen)) {  // outside what the 32-bit ring arithmetic covers
     if (threadIdx.x == 0) set_error(p.err, NSA_ERR_INVALID);

@@ -18,12 +18,16 @@ def test_sweep_columns_and_byte_model(tmp_path):
     assert list(rows[0])[:len(REF_COLS)] == REF_COLS
     assert all(r["ms_sparse"] > 0 and r["ms_dense"] > 0 for r in rows)
     assert rows[1]["predicted_ratio"] == pytest.approx((1_048_576 + 131_072 * 8192) / (1_048_576 + 131_072 * 260))
-    rows_q = benchmark.benchmark_quantized([8192], [0, 256], timer, 6.45, 32)
-    assert [r["W"] for r in rows_q] == [256]  # W < 128 is skipped, as in the reference
+    rows_q = benchmark.benchmark_quantized([8192], [0, 64, 256], timer, 6.45, 32)
+    # W < 128 (skipped by the reference, its benchmark.py:86) runs through the streaming cache
+    assert [(r["W"], r["layout"]) for r in rows_q] == [(64, "stream"), (256, "reference")]
     assert list(rows_q[0])[:len(REF_COLS_Q)] == REF_COLS_Q
-    assert rows_q[0]["bytes_quantized_pred"] == 21_757_952  # the csv's own W=256 figure
+    assert rows_q[0]["ms_quantized"] > 0
+    assert rows_q[0]["bytes_quantized_pred"] == 256 * (3072 + 64 * 512) + 2 * 32 * 64 * 128 * 2
+    assert rows_q[1]["bytes_quantized_pred"] == 21_757_952  # the csv's own W=256 figure
     benchmark.save(rows_q, str(tmp_path / "q.csv"))
     assert (tmp_path / "q.csv").read_text().splitlines()[0].startswith(",".join(REF_COLS_Q))
+    assert benchmark.stream_bytes(32, 32) == 256 * (3072 + 32 * 512) + 1_048_576  # + q and o
 
 
 def test_graph_columns_and_batch_scaling():
