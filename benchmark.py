@@ -130,7 +130,14 @@ def n_copies(nbytes: int) -> int:
 
 
 def randn(*shape, gen):
-    return torch.randn(*shape, generator=gen, device="cuda", dtype=torch.float32).half()
+    return torch.randn(*shape, generator=gen, device="cuda", dtype=torch.float16)
+
+
+def dense_fits(batch: int, L: int) -> bool:
+    """Whether this rank's dense K and V (fp16 [batch, 8, L, 128] each) fit in
+    60% of the device's memory; larger points are recorded as not run (NaN)."""
+    need = 2 * batch * N_KV_HEADS * L * D_HEAD * 2
+    return need <= 0.6 * torch.cuda.get_device_properties(torch.cuda.current_device()).total_memory
 
 
 def benchmark(lengths, windows, timer, peak, batch, gtimer=None):
@@ -142,11 +149,13 @@ def benchmark(lengths, windows, timer, peak, batch, gtimer=None):
     results = []
     for L in lengths:
         q = randn(batch, N_HEADS, D_HEAD, gen=gen)
-        k_dense = randn(batch, N_KV_HEADS, L, D_HEAD, gen=gen)
-        v_dense = randn(batch, N_KV_HEADS, L, D_HEAD, gen=gen)
-        ms_dense = timer(lambda: dense_decode_attention(q, k_dense, v_dense, seq_len=L, sm_scale=sm_scale))
-        gms_dense = None
-        if gtimer:
+        fits = dense_fits(batch, L)
+        k_dense = randn(batch, N_KV_HEADS, L, D_HEAD, gen=gen) if fits else None
+        v_dense = randn(batch, N_KV_HEADS, L, D_HEAD, gen=gen) if fits else None
+        ms_dense = timer(lambda: dense_decode_attention(q, k_dense, v_dense, seq_len=L, sm_scale=sm_scale)) \
+            if fits else float("nan")
+        gms_dense = None if fits else float("nan")
+        if gtimer and fits:
             n = n_copies(2 * k_dense.numel() * 2)
             kv = [(k_dense, v_dense)] + [(k_dense.clone(), v_dense.clone()) for _ in range(n - 1)]
             gms_dense = gtimer([lambda kk=kk, vv=vv: dense_decode_attention(q, kk, vv, seq_len=L, sm_scale=sm_scale)
@@ -209,9 +218,11 @@ def benchmark_quantized(lengths, windows, timer, peak, batch, gtimer=None):
     results = []
     for L in lengths:
         q = randn(batch, N_HEADS, D_HEAD, gen=gen)
-        k_dense = randn(batch, N_KV_HEADS, L, D_HEAD, gen=gen)
-        v_dense = randn(batch, N_KV_HEADS, L, D_HEAD, gen=gen)
-        ms_dense = timer(lambda: dense_decode_attention(q, k_dense, v_dense, seq_len=L, sm_scale=sm_scale))
+        fits = dense_fits(batch, L)
+        k_dense = randn(batch, N_KV_HEADS, L, D_HEAD, gen=gen) if fits else None
+        v_dense = randn(batch, N_KV_HEADS, L, D_HEAD, gen=gen) if fits else None
+        ms_dense = timer(lambda: dense_decode_attention(q, k_dense, v_dense, seq_len=L, sm_scale=sm_scale)) \
+            if fits else float("nan")
         for W in [w for w in windows if w > 0]:
             kc = randn(batch, N_KV_HEADS, SINK_SIZE + W, D_HEAD, gen=gen)
             vc = randn(batch, N_KV_HEADS, SINK_SIZE + W, D_HEAD, gen=gen)

@@ -173,10 +173,6 @@ struct KParams {
   __half* sink_v16;
 };
 
-__device__ __forceinline__ int32_t clampi(int64_t x, int64_t lo, int64_t hi) {
-  return static_cast<int32_t>(x < lo ? lo : (x > hi ? hi : x));
-}
-
 // Per-unit metadata from the unit's length (see nsa_kivi_stream_cache and
 // _kv_indices, sparse_kernel.py:15-46, for the two layouts); `len` is the
 // streaming unit's length (unused for the reference layout).
