@@ -2,6 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload kivi|sparse|dense]
                     [--impl ours|reference] [--no-cpu-baseline] [--headline-only]
+    python bench.py --ncu-workload kivi_ref|ring_step|append|quant   (one small kernel loop for ncu)
 
 A step is one decode-attention pass (one query token per sequence, one layer)
 over a batch of B=32 sequences per GPU with 64 query / 8 KV heads, d=128:
@@ -539,6 +540,57 @@ def e2e_measure(name: str, wl: Workload, a, dev, stream, barrier, max_over_ranks
             "steps": steps}
 
 
+NCU_WORKLOADS = ("kivi_ref", "ring_step", "append", "quant")
+
+
+def ncu_workload(mode: str) -> None:
+    """Small fixed loops of the kernels that the headline does not run, for one
+    ncu capture each (the summaries under profiles/): the reference-layout KIVI
+    attention, the fp16 ring decode step, the split-form append and the set-up
+    quantizers.  No timing, no output line."""
+    import quant_kernel
+
+    pkg = importlib.import_module("numerics-and-sparse-attn_b200")
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(7)
+    b, w = B_PER_GPU, 256
+    if mode == "kivi_ref":  # sparse_decode_attention_quantized over build_quantized_kv_cache, 13 caches in turn
+        keys = ["k_residual", "v_residual", "k_sink_packed", "k_sink_scale", "k_sink_zero", "v_sink_packed",
+                "v_sink_scale", "v_sink_zero", "k_win_packed", "k_win_scale", "k_win_zero", "v_win_packed",
+                "v_win_scale", "v_win_zero"]
+        caches = []
+        for _ in range(13):
+            kc = torch.randn(b, HKV, S + w, D, device=dev, generator=g).half()
+            vc = torch.randn(b, HKV, S + w, D, device=dev, generator=g).half()
+            c = quant_kernel.build_quantized_kv_cache(kc, vc)
+            caches.append([c[k] for k in keys])
+        q = torch.randn(b, H, D, device=dev, generator=g).half()
+        for i in range(26):
+            quant_kernel.sparse_decode_attention_quantized(q, *caches[i % 13], seq_len=163_840, window=w)
+    elif mode == "ring_step":  # RingCache.decode_step (the window kernel's append form), 8 rings in turn
+        rings = []
+        for _ in range(8):
+            r = pkg.RingCache(b, HKV, w, S, device=dev)
+            kh = torch.randn(b, HKV, 1000, D, device=dev, generator=g).half()
+            r.load_history(kh, kh, 1000)
+            rings.append(r)
+        q = torch.randn(b, H, D, device=dev, generator=g).half()
+        nk = torch.randn(b, HKV, D, device=dev, generator=g).half()
+        for i in range(24):
+            rings[i % 8].decode_step(q, nk, nk)
+    elif mode == "append":  # KiviCache.append (kivi_append_kernel), 4 caches in turn, across group flushes
+        caches = [pkg.KiviCache.synthetic(b, HKV, w, 163_840, device=dev, generator=g) for _ in range(4)]
+        nk = torch.randn(b, HKV, D, device=dev, generator=g).half()
+        for i in range(40):
+            caches[i % 4].append(nk, nk)
+    else:  # the set-up quantizers over a 4096-token cache (268 MB of input)
+        k = torch.randn(b, HKV, 4096, D, device=dev, generator=g).half()
+        for _ in range(3):
+            quant_kernel.quantize_k_cache(k)
+            quant_kernel.quantize_v_cache(k)
+    torch.cuda.synchronize()
+
+
 def main():
     quiet_stdout()
     ap = argparse.ArgumentParser()
@@ -549,7 +601,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--headline-only", action="store_true", help="skip the other workloads' sub-objects")
+    ap.add_argument("--ncu-workload", choices=NCU_WORKLOADS,
+                    help="run one small kernel loop for an ncu capture instead of benchmarking")
     a = ap.parse_args()
+    if a.ncu_workload:
+        ncu_workload(a.ncu_workload)
+        return
     a.warmup = max(3, a.warmup)
     a.steps = max(1, a.steps)
 
