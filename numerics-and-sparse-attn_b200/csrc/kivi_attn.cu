@@ -837,6 +837,17 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   if (kRec && has_b0 && threadIdx.x == 0)
     bulk_prefetch_l2(p.grp + unit * (p.n_groups + 1) * int64_t(kRecBytes),
                      static_cast<uint32_t>(min(p.n_groups + 1, kBatchGroups)) * kRecBytes);
+  // Likewise the small inputs every thread loads right after the wait (the
+  // unit's query, length and appended token): their loads then hit L2, which
+  // shortens the prologue on the way to the first group (-0.15 us per step).
+  if (threadIdx.x == 32) {
+    bulk_prefetch_l2(p.q + unit * kGroupHeads * kHeadDim, kGroupHeads * kHeadDim * 2);
+    if (kRec) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.unit_lens + unit));
+    if (kAppend) {
+      bulk_prefetch_l2(p.new_k + unit * kHeadDim, kHeadDim * 2);
+      bulk_prefetch_l2(p.new_v + unit * kHeadDim, kHeadDim * 2);
+    }
+  }
   grid_dependency_wait();
 
   // ------------------------------------------------------------- prologue
@@ -932,6 +943,8 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
           const int r = 32 * j;
           const int r0 = f * kFRows + r;
           const bool two = r + 32 <= kFRows;
+          // the query fragments first: their loads overlap the mask arithmetic below
+          st.load_q(qpad, lane, kQPadStride * 2);  // reloaded here: not held across the quantized path
           bool vl[2], vh[2];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
@@ -943,14 +956,15 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
           if (!any0 && !any1) continue;
           if (ap.f_item == f && ap.f_row >= r && ap.f_row < r + (two ? 32 : 16))  // the appended token's
             patch_residual_row(sd, ap.f_row, smem_u32(sm.newtok), lane);      // staged row is stale
-          st.load_q(qpad, lane, kQPadStride * 2);  // reloaded here: not held across the quantized path
           // V rows of unattended slots become 0 (P is 0 there, and 0 * NaN would not
           // be), except those of a group this launch flushes: it is quantized from them
+          if (!__all_sync(0xffffffffu, vl[0] && vh[0] && (!two || (vl[1] && vh[1])))) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
-            if (h == 0 || two)
-              zero_invalid_v_rows<kRec>(sd + kFTile, r + 16 * h, vl[h] || ap.flushing(r0 + 16 * h + g),
-                                        vh[h] || ap.flushing(r0 + 16 * h + g + 8), lane);
+            for (int h = 0; h < 2; ++h)
+              if (h == 0 || two)
+                zero_invalid_v_rows<kRec>(sd + kFTile, r + 16 * h, vl[h] || ap.flushing(r0 + 16 * h + g),
+                                          vh[h] || ap.flushing(r0 + 16 * h + g + 8), lane);
+          }
           if (two && any0 && any1) {
             st.consume_rows<2, Lay<kRec>::kRowBytes>(sd, sd + kFTile, Lay<kRec>::kRegion, r, vl, vh, p.scale_log2,
                                                      lane);
