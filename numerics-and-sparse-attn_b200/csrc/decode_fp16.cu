@@ -389,6 +389,18 @@ __global__ void __launch_bounds__(win::kThreads, 2)
       tma_prefetch_4d(&tmK, 0, i * win::kRows, 0, static_cast<int>(unit));
       tma_prefetch_4d(&tmV, 0, i * win::kRows, 0, static_cast<int>(unit));
     }
+  // likewise the small inputs loaded right after the wait (query, lengths, ring
+  // heads, appended token), so that those loads hit L2
+  if (ct == 32) {
+    bulk_prefetch_l2(p.q + unit * kGroupHeads * kHeadDim, kGroupHeads * kHeadDim * 2);
+    if (p.unit_lens) prefetch_l2(p.unit_lens + unit);
+    if (p.seq_lens) prefetch_l2(p.seq_lens + unit / p.n_kv_heads);
+    if (p.ring_heads) prefetch_l2(p.ring_heads + unit / p.n_kv_heads);
+    if (appending) {
+      bulk_prefetch_l2(p.new_k + unit * kHeadDim, kHeadDim * 2);
+      bulk_prefetch_l2(p.new_v + unit * kHeadDim, kHeadDim * 2);
+    }
+  }
   grid_dependency_wait();
 
   // Tile i uses stage i % kStages; it is issued once warp 0 itself has

@@ -842,7 +842,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   // shortens the prologue on the way to the first group (-0.15 us per step).
   if (threadIdx.x == 32) {
     bulk_prefetch_l2(p.q + unit * kGroupHeads * kHeadDim, kGroupHeads * kHeadDim * 2);
-    if (kRec) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.unit_lens + unit));
+    if (kRec) prefetch_l2(p.unit_lens + unit);
     if (kAppend) {
       bulk_prefetch_l2(p.new_k + unit * kHeadDim, kHeadDim * 2);
       bulk_prefetch_l2(p.new_v + unit * kHeadDim, kHeadDim * 2);
