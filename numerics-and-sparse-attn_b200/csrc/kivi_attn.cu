@@ -230,11 +230,26 @@ __device__ __forceinline__ uint32_t group_mask(const KParams& p, const KiviMeta&
   return ~((1u << first) - 1u);
 }
 
-__device__ __forceinline__ bool res_slot_valid(const KParams& p, const KiviMeta& m, int r) {
-  if (r >= p.res_cap) return false;
-  int d = r - m.res_head;
-  if (d < 0) d += p.res_cap;
-  return d >= m.res_skip && d < m.n_res;
+// Bits [lo, hi) of a 32-bit word (bounds clamped to [0, 32]).
+__device__ __forceinline__ uint32_t bit_range(int lo, int hi) {
+  lo = max(lo, 0);
+  hi = min(hi, 32);
+  if (lo >= hi) return 0u;
+  const uint32_t below_hi = hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u);
+  return below_hi & ~((1u << lo) - 1u);
+}
+
+// Attended residual slots r0 .. r0 + 31 as a mask (bit i: slot r0 + i),
+// computed with warp-uniform integer arithmetic: a slot below res_cap sits
+// d = (slot - res_head) mod res_cap from the oldest live slot and is attended
+// iff res_skip <= d < n_res; slots from res_cap on do not exist.
+__device__ __forceinline__ uint32_t res_slot_mask(const KParams& p, const KiviMeta& m, int r0) {
+  const int C = p.res_cap;
+  int a = r0 - m.res_head;  // d of slot r0 (before the wrap below)
+  if (a < 0) a += C;
+  uint32_t mk = bit_range(m.res_skip - a, m.n_res - a) & bit_range(0, C - a);  // d = a + i
+  mk |= bit_range(m.res_skip + C - a, m.n_res + C - a) & bit_range(C - a, 32);  // d = a + i - C
+  return mk & bit_range(0, C - r0);  // slots >= res_cap do not exist
 }
 
 // Whether Q-batch b holds any attended token.  Batch 0 counts as live always:
@@ -945,20 +960,21 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
           const bool two = r + 32 <= kFRows;
           // the query fragments first: their loads overlap the mask arithmetic below
           st.load_q(qpad, lane, kQPadStride * 2);  // reloaded here: not held across the quantized path
+          // attended rows of the job (warp-uniform mask; bit i: row r + i)
+          const uint32_t vm = res_slot_mask(p, meta, r0) & (two ? 0xffffffffu : 0xffffu);
+          if (!vm) continue;
           bool vl[2], vh[2];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            vl[h] = (h == 0 || two) && res_slot_valid(p, meta, r0 + 16 * h + g);
-            vh[h] = (h == 0 || two) && res_slot_valid(p, meta, r0 + 16 * h + g + 8);
+            vl[h] = ((vm >> (16 * h + g)) & 1u) != 0;
+            vh[h] = ((vm >> (16 * h + g + 8)) & 1u) != 0;
           }
-          const bool any0 = __any_sync(0xffffffffu, vl[0] || vh[0]);
-          const bool any1 = __any_sync(0xffffffffu, vl[1] || vh[1]);
-          if (!any0 && !any1) continue;
+          const bool any0 = (vm & 0xffffu) != 0, any1 = (vm >> 16) != 0;
           if (ap.f_item == f && ap.f_row >= r && ap.f_row < r + (two ? 32 : 16))  // the appended token's
             patch_residual_row(sd, ap.f_row, smem_u32(sm.newtok), lane);      // staged row is stale
           // V rows of unattended slots become 0 (P is 0 there, and 0 * NaN would not
           // be), except those of a group this launch flushes: it is quantized from them
-          if (!__all_sync(0xffffffffu, vl[0] && vh[0] && (!two || (vl[1] && vh[1])))) {
+          if (vm != (two ? 0xffffffffu : 0xffffu)) {
 #pragma unroll
             for (int h = 0; h < 2; ++h)
               if (h == 0 || two)
