@@ -32,6 +32,15 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
+// Bits [lo, hi) of a 32-bit word (bounds clamped to [0, 32]).
+__device__ __forceinline__ uint32_t bit_range(int lo, int hi) {
+  lo = max(lo, 0);
+  hi = min(hi, 32);
+  if (lo >= hi) return 0u;
+  const uint32_t below_hi = hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u);
+  return below_hi & ~((1u << lo) - 1u);
+}
+
 // Record the first error of a launch; later errors keep the first code.
 __device__ __forceinline__ void set_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);

@@ -126,6 +126,25 @@ __device__ __forceinline__ bool slot_valid(const Params& p, int64_t slot, const 
   return x >= m.n_inv;
 }
 
+// Valid slots r0 .. r0 + 31 of a sink+window cache as a mask (bit i: slot
+// r0 + i), the set slot_valid gives, from warp-uniform arithmetic.  Needs
+// window >= 32, so that 32 consecutive slots wrap the ring at most once.
+__device__ __forceinline__ uint32_t window_slot_mask(const Params& p, int r0, const PieceMeta& m) {
+  const int S = p.sink, W = p.window;
+  const int ns = m.len < S ? static_cast<int>(m.len) : S;  // sink slots s < min(S, len)
+  uint32_t mk = bit_range(0, ns - r0);
+  const int i0 = max(S - r0, 0);  // bit of the first window slot in the range
+  if (i0 < 32) {
+    int a = r0 + i0 - S - m.head;  // in (-W, W)
+    if (a < 0) a += W;             // logical index of slot r0 + i0
+    const int wrap = i0 + W - a;   // first bit whose logical index wraps to 0
+    mk |= bit_range(i0 + m.n_inv - a, wrap) & bit_range(i0, 32);  // index a + i - i0 >= n_inv
+    mk |= bit_range(wrap + m.n_inv, 32);                           // index i - wrap >= n_inv
+    mk &= bit_range(0, S + W - r0);                                // slots >= S + W do not exist
+  }
+  return mk;
+}
+
 // Number of tiles of `unit` that can hold a valid slot (dense: up to len).
 __device__ __forceinline__ int64_t unit_tiles(const Params& p, int64_t unit) {
   if (p.mode == kDense && !p.unit_lens) {
@@ -466,15 +485,17 @@ __global__ void __launch_bounds__(win::kThreads, 2)
     for (int jj = wclaim(&sm.job[s], lane); jj < win::kRows / 32; jj = wclaim(&sm.job[s], lane)) {
       const int r = 32 * jj;
       const int64_t r0 = int64_t(ti) * win::kRows + r;
+      // valid rows of the job (bit i: row r + i): uniform arithmetic, or one vote for windows below 32
+      const uint32_t vm = p.window >= 32 ? window_slot_mask(p, static_cast<int>(r0), meta)
+                                         : __ballot_sync(0xffffffffu, slot_valid(p, r0 + lane, meta));
+      if (!vm) continue;
       bool vl[2], vh[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        vl[h] = slot_valid(p, r0 + 16 * h + g, meta);
-        vh[h] = slot_valid(p, r0 + 16 * h + g + 8, meta);
+        vl[h] = ((vm >> (16 * h + g)) & 1u) != 0;
+        vh[h] = ((vm >> (16 * h + g + 8)) & 1u) != 0;
       }
-      const bool any0 = __any_sync(0xffffffffu, vl[0] || vh[0]);
-      const bool any1 = __any_sync(0xffffffffu, vl[1] || vh[1]);
-      if (!any0 && !any1) continue;
+      const bool any0 = (vm & 0xffffu) != 0, any1 = (vm >> 16) != 0;
       if (aslot >= r0 && aslot < r0 + 32) {  // the appended token's staged row is stale
         const int row = aslot - ti * win::kRows, kv = lane >> 4, chunk = lane & 15;
         uint4 x = *reinterpret_cast<const uint4*>(&sm.newtok[kv][chunk * 8]);

@@ -230,15 +230,6 @@ __device__ __forceinline__ uint32_t group_mask(const KParams& p, const KiviMeta&
   return ~((1u << first) - 1u);
 }
 
-// Bits [lo, hi) of a 32-bit word (bounds clamped to [0, 32]).
-__device__ __forceinline__ uint32_t bit_range(int lo, int hi) {
-  lo = max(lo, 0);
-  hi = min(hi, 32);
-  if (lo >= hi) return 0u;
-  const uint32_t below_hi = hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u);
-  return below_hi & ~((1u << lo) - 1u);
-}
-
 // Attended residual slots r0 .. r0 + 31 as a mask (bit i: slot r0 + i),
 // computed with warp-uniform integer arithmetic: a slot below res_cap sits
 // d = (slot - res_head) mod res_cap from the oldest live slot and is attended
@@ -943,6 +934,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
     const int phase = (f_first && step < 2) ? 1 - step : step;
     if (phase == 3 && !defer_slot) break;
     if (phase == 1) {
+      st.load_q(qpad, lane, kQPadStride * 2);  // the residual jobs' query fragments (not held across the groups)
 #pragma unroll 1
       for (int f = f_begin; f < f_end; ++f) {
         if (leader) iss.pump_f(nf);
@@ -958,8 +950,6 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
           const int r = 32 * j;
           const int r0 = f * kFRows + r;
           const bool two = r + 32 <= kFRows;
-          // the query fragments first: their loads overlap the mask arithmetic below
-          st.load_q(qpad, lane, kQPadStride * 2);  // reloaded here: not held across the quantized path
           // attended rows of the job (warp-uniform mask; bit i: row r + i)
           const uint32_t vm = res_slot_mask(p, meta, r0) & (two ? 0xffffffffu : 0xffffu);
           if (!vm) continue;
