@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload kivi|sparse|dense]
                     [--impl ours|reference] [--no-cpu-baseline] [--headline-only]
-    python bench.py --ncu-workload kivi_ref|ring_step|append|quant   (one small kernel loop for ncu)
+    python bench.py --ncu-workload kivi_step|sparse|kivi_ref|ring_step|append|quant   (kernel loop for ncu)
 
 A step is one decode-attention pass (one query token per sequence, one layer)
 over a batch of B=32 sequences per GPU with 64 query / 8 KV heads, d=128:
@@ -86,8 +86,8 @@ def algorithmic_bytes(workload: str, batch: int) -> int:
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of ONE launch of the
 # dominant kernel at B=32, from the committed ncu captures of this exact workload.
 NCU_TRAFFIC = {
-    "kivi": (25_626_624, "profiles/kivi_stream_step_kernel_kivi_W256_L163840_B32.md"),
-    "sparse": (34_632_960, "profiles/window_decode_kernel_sparse_W256_L163840_B32.md"),
+    "kivi": (25_630_208, "profiles/kivi_stream_step_kernel_kivi_W256_L163840_B32.md"),
+    "sparse": (34_633_984, "profiles/window_decode_kernel_sparse_W256_L163840_B32.md"),
     "dense": (1_078_491_176, "profiles/fp16_decode_kernel_dense_L8192_B32.md"),
 }
 
@@ -504,14 +504,18 @@ def e2e_measure(name: str, wl: Workload, a, dev, stream, barrier, max_over_ranks
             o = wl.step(i, views[0])
         o_h[0].copy_(o, non_blocking=True)
 
+    host_ms = {}
+
     def timed(call, piped):
         barrier()
         torch.cuda.synchronize()
         e0.record(stream)
         if piped:
             pipe.begin()
+        t0 = time.perf_counter()
         for i in range(steps):
             call(i)
+        host_ms[piped] = (time.perf_counter() - t0) * 1e3 / steps  # host time to issue one step
         if piped:
             pipe.end()
         e1.record(stream)
@@ -536,25 +540,30 @@ def e2e_measure(name: str, wl: Workload, a, dev, stream, barrier, max_over_ranks
         pipe.close()
         h2d_ms = max_over_ranks(copy_rate(x_d, x_h))
         d2h_ms = max_over_ranks(copy_rate(o_h[0], [o_d]))
-    return {"ms": e2e_ms, "serial_ms": serial_ms, "h2d": h2d, "d2h": d2h, "h2d_ms": h2d_ms, "d2h_ms": d2h_ms,
+    return {"ms": e2e_ms, "serial_ms": serial_ms, "host_issue_ms": host_ms[True], "h2d": h2d, "d2h": d2h, "h2d_ms": h2d_ms, "d2h_ms": d2h_ms,
             "steps": steps}
 
 
-NCU_WORKLOADS = ("kivi_ref", "ring_step", "append", "quant")
+NCU_WORKLOADS = ("kivi_step", "sparse", "kivi_ref", "ring_step", "append", "quant")
 
 
 def ncu_workload(mode: str) -> None:
-    """Small fixed loops of the kernels that the headline does not run, for one
-    ncu capture each (the summaries under profiles/): the reference-layout KIVI
-    attention, the fp16 ring decode step, the split-form append and the set-up
-    quantizers.  No timing, no output line."""
+    """Small fixed loops of the decode kernels, for one ncu capture each (the
+    summaries under profiles/): the headline KIVI step and the sink+window
+    attention over the bench's layer rotations (30 steps), the
+    reference-layout KIVI attention, the fp16 ring decode step, the split-form
+    append and the set-up quantizers.  No timing, no output line."""
     import quant_kernel
 
     pkg = importlib.import_module("numerics-and-sparse-attn_b200")
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(7)
     b, w = B_PER_GPU, 256
-    if mode == "kivi_ref":  # sparse_decode_attention_quantized over build_quantized_kv_cache, 13 caches in turn
+    if mode in ("kivi_step", "sparse"):  # the bench's own workloads (layer rotations > 2x L2), 30 steps
+        wl = Workload("kivi" if mode == "kivi_step" else "sparse", b, dev, seed=1234)
+        for i in range(30):
+            wl.step(i)
+    elif mode == "kivi_ref":  # sparse_decode_attention_quantized over build_quantized_kv_cache, 13 caches in turn
         keys = ["k_residual", "v_residual", "k_sink_packed", "k_sink_scale", "k_sink_zero", "v_sink_packed",
                 "v_sink_scale", "v_sink_zero", "k_win_packed", "k_win_scale", "k_win_zero", "v_win_packed",
                 "v_win_scale", "v_win_zero"]
@@ -719,7 +728,8 @@ def main():
                 "h2d_gbs": e2e["h2d"] / (e2e["h2d_ms"] * 1e-3) / 1e9,
                 "d2h_gbs": e2e["d2h"] / (e2e["d2h_ms"] * 1e-3) / 1e9,
                 "bound_ms": e2e_bound, "ms_over_bound": e2e["ms"] / e2e_bound,
-                "device_api_serial_ms_per_step": e2e["serial_ms"]},
+                "device_api_serial_ms_per_step": e2e["serial_ms"],
+                "host_issue_ms_per_step": e2e["host_issue_ms"]},
         "gpu_launches": a.steps * launches,
         **({"layer_batched": {
             "layers_per_launch": wl.n_layers, "us_per_layer_step": head["layered_ms"] * 1e3,
