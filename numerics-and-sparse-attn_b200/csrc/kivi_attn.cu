@@ -844,7 +844,7 @@ struct Issuer {
 // The work of CTA `bid` of one layer's launch (tensor maps -- reference
 // layout only -- and parameters in kernel-parameter space).  kAppend: the
 // launch also appends new_k / new_v (streaming layout, one CTA per unit).
-template <bool kRec, bool kAppend, bool kSized = false>
+template <bool kRec, bool kAppend, bool kSized, bool kSimple>
 __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CUtensorMap* tmV, const KParams& p,
                                                 int bid) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -975,7 +975,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   // flushed slot waits until after the F-tiles (step 3); otherwise the
   // F-tiles come first and the group is read from the cache.
   const bool flushing = ap.fl_batch >= 0;
-  const bool resident = p.n_qb <= kQStages && p.n_ft <= kFStages && f_begin == 0 && f_end == p.n_ft;
+  const bool resident = kSimple || (p.n_qb <= kQStages && p.n_ft <= kFStages && f_begin == 0 && f_end == p.n_ft);
   const bool defer_slot = flushing && resident && ap.fl_batch == 0;
   const bool f_first = flushing && !resident;
 #pragma unroll 1
@@ -986,7 +986,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
       st.load_q(qpad, lane, kQPadStride * 2);  // the residual jobs' query fragments (not held across the groups)
 #pragma unroll 1
       for (int f = f_begin; f < f_end; ++f) {
-        if (leader) iss.pump_f(nf);
+        if (!kSimple && leader) iss.pump_f(nf);
         __syncwarp();
         const uint32_t s = nf % kFStages, ph = (nf / kFStages) & 1;
         ++nf;
@@ -1031,7 +1031,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&sm.f_empty[s]));
+        if (!kSimple && lane == 0) mbar_arrive(smem_u32(&sm.f_empty[s]));
       }
       continue;
     }
@@ -1042,7 +1042,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
       if (!batch_live(p, meta, b)) continue;
       uint32_t qs, s = 0;
       if (phase != 3) {
-        if (leader) iss.pump_f(nf);
+        if (!kSimple && leader) iss.pump_f(nf);
         __syncwarp();
         s = nq % kQStages;
         const uint32_t ph = (nq / kQStages) & 1;
@@ -1075,7 +1075,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
         if (!mask) continue;
         attend_group<kRec>(st, qrow, lq, qs, gs, mask, p.scale_log2, lane);
       }
-      if (phase != 3) {  // release the stage; the last warp to do so refills it
+      if (!kSimple && phase != 3) {  // release the stage; the last warp to do so refills it
         __syncwarp();
         if (lane == 0) {
           __threadfence_block();  // this warp's reads of the stage come first
@@ -1118,7 +1118,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
       p.unit_lens[unit] = len;
   }
   __half* out = p.o + unit * kGroupHeads * kHeadDim;
-  if (p.ppu == 1) {
+  if (kSimple || p.ppu == 1) {
     store_half8(out + hh * kHeadDim + d0, o);
     return;
   }
@@ -1140,11 +1140,17 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   }
 }
 
+// kSimple: one CTA per unit and every item resident in its stage from the
+// start (at most kQStages Q-batches and kFStages F-tiles), so nothing is ever
+// refilled and no piece is merged: the refill and split-K code is left out
+// of this instantiation (W=256 step 7.75 -> 7.62 us, W=32 5.65 -> 5.05 us at B=32).
+//
 // The reference's 14-tensor layout (residual by TMA boxes).
+template <bool kSimple>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     kivi_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                        const KParams p) {
-  kivi_decode_cta<false, false>(&tmK, &tmV, p, blockIdx.x);
+  kivi_decode_cta<false, false, false, kSimple>(&tmK, &tmV, p, blockIdx.x);
 }
 
 // The streaming cache (every load a 1-D bulk copy): attention only, and a
@@ -1154,14 +1160,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 // unit's length is known): W=32 6.7 -> 5.7 us, W=64 6.8 -> 6.1 us per launch
 // at B=32.  Longer windows attend nearly every slot and keep the copies that
 // need no length, in their own instantiation.
-template <bool kSized>
+template <bool kSized, bool kSimple>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) kivi_stream_decode_kernel(const KParams p) {
-  kivi_decode_cta<true, false, kSized>(nullptr, nullptr, p, blockIdx.x);
+  kivi_decode_cta<true, false, kSized, kSimple>(nullptr, nullptr, p, blockIdx.x);
 }
-template <bool kSized>
+template <bool kSized, bool kSimple>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     kivi_stream_step_kernel(const __grid_constant__ KParams p) {
-  kivi_decode_cta<true, true, kSized>(nullptr, nullptr, p, blockIdx.x);
+  kivi_decode_cta<true, true, kSized, kSimple>(nullptr, nullptr, p, blockIdx.x);
 }
 
 // Several layers (caches of one geometry) in one launch: layer-major CTAs,
@@ -1176,11 +1182,20 @@ struct KiviLayers {
 };
 static_assert(sizeof(KiviLayers) <= 32000, "kernel parameter space");
 
-template <bool kSized>
+template <bool kSized, bool kSimple>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) kivi_decode_layers_kernel(const __grid_constant__ KiviLayers L) {
   const int layer = static_cast<int>(blockIdx.x / L.per_layer);
-  kivi_decode_cta<true, true, kSized>(nullptr, nullptr, L.p[layer], static_cast<int>(blockIdx.x % L.per_layer));
+  kivi_decode_cta<true, true, kSized, kSimple>(nullptr, nullptr, L.p[layer],
+                                              static_cast<int>(blockIdx.x % L.per_layer));
 }
+
+// One of a kernel's four instantiations <kSized, kSimple>.
+template <class K>
+K pick(bool sized, bool simple, K ff, K ft, K tf, K tt) {
+  return sized ? (simple ? tt : tf) : (simple ? ft : ff);
+}
+#define NSA_KIVI_PICK(kernel, sized, simple) \
+  pick(sized, simple, kernel<false, false>, kernel<false, true>, kernel<true, false>, kernel<true, true>)
 
 // Whether a streaming-cache launch sizes its F-tile copies (see above).
 bool sized_f(const KParams& p) { return p.layout == 1 && p.window < p.residual; }
@@ -1204,10 +1219,12 @@ int64_t cta_slots() {
       return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)) ==
              cudaSuccess;
     };
-    if (!smem(kivi_decode_kernel) || !smem(kivi_stream_decode_kernel<false>) || !smem(kivi_stream_decode_kernel<true>) ||
-        !smem(kivi_stream_step_kernel<false>) || !smem(kivi_stream_step_kernel<true>) ||
-        !smem(kivi_decode_layers_kernel<false>) || !smem(kivi_decode_layers_kernel<true>) ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kivi_decode_kernel, kThreads, kSmemBytes) !=
+    bool ok = smem(kivi_decode_kernel<false>) && smem(kivi_decode_kernel<true>);
+    for (int i = 0; i < 4; ++i)
+      ok = ok && smem(NSA_KIVI_PICK(kivi_stream_decode_kernel, i & 1, i >> 1)) &&
+           smem(NSA_KIVI_PICK(kivi_stream_step_kernel, i & 1, i >> 1)) &&
+           smem(NSA_KIVI_PICK(kivi_decode_layers_kernel, i & 1, i >> 1));
+    if (!ok || cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kivi_decode_kernel<false>, kThreads, kSmemBytes) !=
             cudaSuccess ||
         per_sm < 1) {
       cudaGetLastError();
@@ -1233,6 +1250,9 @@ Plan plan(int64_t n_units, int n_groups, int res_cap) {
   s.grid = n_units * ppu;
   return s;
 }
+
+// Whether a launch of plan s can take the kSimple instantiation.
+bool simple(const Plan& s) { return s.ppu == 1 && s.n_qb <= kQStages && s.n_ft <= kFStages; }
 
 size_t ws_bytes(const Plan& s) {
   const size_t counters = ((s.n_units * sizeof(int)) + 255) & ~size_t(255);
@@ -1284,13 +1304,13 @@ int launch(KParams& p, const Plan& s, const void* k_res, const void* v_res, void
   if (rc) return rc;
   cta_slots();  // sets the shared-memory limit
   const dim3 grid(static_cast<unsigned>(s.grid));
-  const bool sz = sized_f(p);
+  const bool sz = sized_f(p), sp = simple(s);
   cudaError_t e =
-      p.layout == 0 ? launch_kernel(kivi_decode_kernel, grid, dim3(kThreads), kSmemBytes, stream, mk, mv, p)
-      : p.new_k     ? launch_kernel(sz ? kivi_stream_step_kernel<true> : kivi_stream_step_kernel<false>, grid,
-                                    dim3(kThreads), kSmemBytes, stream, p)
-                    : launch_kernel(sz ? kivi_stream_decode_kernel<true> : kivi_stream_decode_kernel<false>, grid,
-                                    dim3(kThreads), kSmemBytes, stream, p);
+      p.layout == 0 ? launch_kernel(sp ? kivi_decode_kernel<true> : kivi_decode_kernel<false>, grid, dim3(kThreads),
+                                    kSmemBytes, stream, mk, mv, p)
+      : p.new_k ? launch_kernel(NSA_KIVI_PICK(kivi_stream_step_kernel, sz, sp), grid, dim3(kThreads), kSmemBytes, stream, p)
+                : launch_kernel(NSA_KIVI_PICK(kivi_stream_decode_kernel, sz, sp), grid, dim3(kThreads), kSmemBytes,
+                                stream, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? NSA_OK : cuda_fail(e, "kivi decode launch");
 }
@@ -1510,7 +1530,7 @@ int nsa_kivi_stream_decode_step_layers(const nsa_kivi_stream_cache* caches, int6
     }
     L.per_layer = s.grid;
     L.n_layers = n;
-    cudaError_t e = launch_kernel(sized_f(L.p[0]) ? kivi_decode_layers_kernel<true> : kivi_decode_layers_kernel<false>,
+    cudaError_t e = launch_kernel(NSA_KIVI_PICK(kivi_decode_layers_kernel, sized_f(L.p[0]), simple(s)),
                                   dim3(static_cast<unsigned>(s.grid * n)), dim3(kThreads), kSmemBytes, stream, L);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "kivi_decode_layers_kernel launch");
