@@ -1241,9 +1241,13 @@ Plan plan(int64_t n_units, int n_groups, int res_cap) {
   s.n_qb = (n_groups + 1 + kBatchGroups - 1) / kBatchGroups;
   s.n_ft = (res_cap + kFRows - 1) / kFRows;
   s.items = s.n_qb + s.n_ft;
-  // fewer units than CTA slots: split each unit's items so that the slots fill
+  // fewer units than CTA slots: split each unit's items so that the slots
+  // fill -- unless every item of a unit is resident in its stages from the
+  // start: such a unit is a short chain whose split pieces would only add the
+  // merge (and, for a decode step, a separate append launch)
   const int64_t slots = cta_slots();
-  int64_t ppu = (n_units > 0 && n_units < slots) ? slots / n_units : 1;
+  const bool resident = s.n_qb <= kQStages && s.n_ft <= kFStages;
+  int64_t ppu = (!resident && n_units > 0 && n_units < slots) ? slots / n_units : 1;
   if (ppu > s.items) ppu = s.items;
   if (ppu < 1) ppu = 1;
   s.ppu = static_cast<int>(ppu);
