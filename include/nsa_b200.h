@@ -112,8 +112,8 @@ int nsa_sparse_decode(const void* q, const void* k_cache, const void* v_cache, v
  * nsa_sparse_decode's.  nsa_ring_append stores one token per unit (new_k,
  * new_v f16 [B, Hkv, D]) and advances unit_lens; nsa_ring_decode attends
  * (workspace: nsa_sparse_workspace_bytes); nsa_ring_decode_step does both,
- * in one launch when every unit has its own CTA (at least one unit per SM and
- * sink + window <= 384), else as append + decode. */
+ * in one launch when every unit has its own CTA (sink + window <= 384), else
+ * as append + decode. */
 int nsa_ring_append(void* k_cache, void* v_cache, int64_t* unit_lens, const void* new_k, const void* new_v,
                     int64_t batch, int64_t n_kv_heads, int64_t head_dim, int64_t window, int64_t sink,
                     nsa_stream_t stream);

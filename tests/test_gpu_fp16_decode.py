@@ -125,11 +125,12 @@ def test_sparse_reference_cases_full_batch(L, W):
     assert _err(o2, ref) < TOL
 
 
-@pytest.mark.parametrize("B,W", [(6, 256), (30, 256), (24, 380), (20, 60)])
+@pytest.mark.parametrize("B,W", [(6, 1020), (6, 256), (30, 256), (24, 380), (20, 60)])
 def test_sparse_ragged_per_sequence_lengths(B, W):
     """Per-sequence seq_lens and ring heads: each row equals a B=1 call
-    (B=6: the persistent kernel; B >= 19, i.e. >= 148 units: one CTA per unit,
-    with W + S = 260 / 384 / 64 slots in 3 / 4 / 1 tiles)."""
+    (W=1020: the persistent kernel, units split over the SMs; W + S <= 384:
+    one CTA per unit at any batch, with 260 / 384 / 64 slots in 3 / 4 / 1
+    tiles, and 48 units -- fewer than the SMs -- at B=6)."""
     S = 4
     lens = ([1, 3, 100, 260, 261, 5000] * 6)[:B]
     lens = [L + (i // 6) * 7 for i, L in enumerate(lens)]

@@ -61,10 +61,11 @@ def _check_twice(B, W, L, seed, S=4, ring=False):
     assert importlib.import_module("numerics-and-sparse-attn_b200").device_error() == 0
 
 
-@pytest.mark.parametrize("B,W,L", [(2, 256, 5000), (3, 1024, 600), (4, 4096, 10_000)])
+@pytest.mark.parametrize("B,W,L", [(2, 512, 5000), (3, 1024, 600), (4, 4096, 10_000)])
 def test_noalloc_split_units_twice(B, W, L):
-    """Fewer units than SMs: each unit is split over several CTAs, whose
-    tickets and partials live in the static scratch."""
+    """Fewer units than SMs and windows beyond the window kernel's 384 slots:
+    each unit is split over several CTAs, whose tickets and partials live in
+    the static scratch."""
     _check_twice(B, W, L, seed=B * 7 + W)
 
 
