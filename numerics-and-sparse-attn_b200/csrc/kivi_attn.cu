@@ -946,7 +946,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   const AppendPlan ap = appending && len64 == len ? append_plan(p, len) : AppendPlan{};
   if (appending && len64 == len) ++len;
   const KiviMeta meta = make_meta<kRec>(p, len);
-  if (leader) iss.pump_q(meta, 0);
+  if (!kSimple && leader) iss.pump_q(meta, 0);
   if (kRec && kSized && lane == 0 && warp >= 1)
     for (int i = warp - 1; i < kFStages; i += kCWarps - 1) iss.first_f_sized(i, meta, ap.fl_s0);
   sts128(smem_u32(&sm.qpad[ct >> 4][(ct & 15) * 8]), qv.x, qv.y, qv.z, qv.w);
@@ -1035,6 +1035,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
       }
       continue;
     }
+    if (kSimple && phase == 2) continue;  // one Q-batch
     const int lo = phase == 2 ? b_begin : 0;
     const int hi = phase == 2 ? b_end : (phase == 3 || has_b0 ? 1 : 0);
 #pragma unroll 1
@@ -1140,10 +1141,11 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   }
 }
 
-// kSimple: one CTA per unit and every item resident in its stage from the
-// start (at most kQStages Q-batches and kFStages F-tiles), so nothing is ever
-// refilled and no piece is merged: the refill and split-K code is left out
-// of this instantiation (W=256 step 7.75 -> 7.62 us, W=32 5.65 -> 5.05 us at B=32).
+// kSimple: one CTA per unit, one Q-batch and every F-tile resident in its
+// stage from the start, so nothing is ever refilled and no piece is merged:
+// the refill, later-batch and split-K code is left out of this instantiation
+// (B=32: W=256 step 7.75 -> 7.61 us, reference-layout launch -0.35 us, W=32
+// 5.65 -> 4.95 us).
 //
 // The reference's 14-tensor layout (residual by TMA boxes).
 template <bool kSimple>
@@ -1256,7 +1258,7 @@ Plan plan(int64_t n_units, int n_groups, int res_cap) {
 }
 
 // Whether a launch of plan s can take the kSimple instantiation.
-bool simple(const Plan& s) { return s.ppu == 1 && s.n_qb <= kQStages && s.n_ft <= kFStages; }
+bool simple(const Plan& s) { return s.ppu == 1 && s.n_qb == 1 && s.n_ft <= kFStages; }
 
 size_t ws_bytes(const Plan& s) {
   const size_t counters = ((s.n_units * sizeof(int)) + 255) & ~size_t(255);
