@@ -844,7 +844,7 @@ struct Issuer {
 // The work of CTA `bid` of one layer's launch (tensor maps -- reference
 // layout only -- and parameters in kernel-parameter space).  kAppend: the
 // launch also appends new_k / new_v (streaming layout, one CTA per unit).
-template <bool kRec, bool kAppend, bool kSized, bool kSimple>
+template <bool kRec, bool kAppend, bool kSized, bool kSimple, bool kLateTile1 = false>
 __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CUtensorMap* tmV, const KParams& p,
                                                 int bid) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -936,8 +936,9 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   // streaming layout: the free stages' F-tiles, one warp each: their copies are issued while
   // lane 0 of warp 0 issues batch 0 (each copy request takes hundreds of cycles to issue):
   // -0.1 to -0.2 us.  (The reference layout's tile loads need the tensor maps lane 0 prefetches.)
+  // (kLateTile1: F-tile 1 waits for the length below and covers only the rows read)
   if (kRec && !kSized && lane == 0 && warp >= 1)
-    for (int i = warp - 1; i < kFStages; i += kCWarps - 1) iss.first_f(i);
+    for (int i = warp - 1; i < (kLateTile1 ? 1 : kFStages); i += kCWarps - 1) iss.first_f(i);
   int len = static_cast<int>(len64);
   if (kRec && (len64 < 0 || len64 >= kMaxUnitLen)) {  // outside what the 32-bit ring arithmetic covers
     if (threadIdx.x == 0) set_error(p.err, NSA_ERR_INVALID);
@@ -949,6 +950,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   if (!kSimple && leader) iss.pump_q(meta, 0);
   if (kRec && kSized && lane == 0 && warp >= 1)
     for (int i = warp - 1; i < kFStages; i += kCWarps - 1) iss.first_f_sized(i, meta, ap.fl_s0);
+  if (kRec && !kSized && kLateTile1 && lane == 0 && warp == 2) iss.first_f_sized(1, meta, ap.fl_s0);
   sts128(smem_u32(&sm.qpad[ct >> 4][(ct & 15) * 8]), qv.x, qv.y, qv.z, qv.w);
   if (appending) {
     sm.newtok[0][ct] = new_kc;
@@ -1162,14 +1164,20 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 // unit's length is known): W=32 6.7 -> 5.7 us, W=64 6.8 -> 6.1 us per launch
 // at B=32.  Longer windows attend nearly every slot and keep the copies that
 // need no length, in their own instantiation.
+//
+// A one-layer launch copies F-tile 1 (the second 80 slots) only once the
+// unit's length is known, and only the rows it reads: F-tile 0 and batch 0
+// keep DRAM busy meanwhile (W=256 step 7.59 -> 7.43 us, DRAM bytes -1 MB).
+// The layer-batched launch keeps the blind copy (there the wait measured
+// +0.19 us per layer).
 template <bool kSized, bool kSimple>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) kivi_stream_decode_kernel(const KParams p) {
-  kivi_decode_cta<true, false, kSized, kSimple>(nullptr, nullptr, p, blockIdx.x);
+  kivi_decode_cta<true, false, kSized, kSimple, true>(nullptr, nullptr, p, blockIdx.x);
 }
 template <bool kSized, bool kSimple>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     kivi_stream_step_kernel(const __grid_constant__ KParams p) {
-  kivi_decode_cta<true, true, kSized, kSimple>(nullptr, nullptr, p, blockIdx.x);
+  kivi_decode_cta<true, true, kSized, kSimple, true>(nullptr, nullptr, p, blockIdx.x);
 }
 
 // Several layers (caches of one geometry) in one launch: layer-major CTAs,
