@@ -134,7 +134,8 @@ int nsa_ring_decode_step(const void* q, void* k_cache, void* v_cache, void* o,
  * caller without a device allocator.  The split-K scratch lives in a static
  * 4 MiB device array inside this library (held by every GPU that loads it
  * until exit).  Only launches that split a unit over several CTAs use it
- * (fewer units than SMs, or windows long enough for stream-K); those whose
+ * (caches of more than 384 slots with fewer units than SMs, or long enough
+ * for stream-K); those whose
  * scratch does not fit are rejected with NSA_ERR_UNSUPPORTED, while shapes
  * that keep every unit whole (one unit per CTA) have no size limit.  The
  * first call on a device that needs the array looks it up and clears it --
@@ -244,7 +245,9 @@ int nsa_kivi_stream_decode(const nsa_kivi_stream_cache* cache, const void* q, vo
                            void* workspace, size_t workspace_bytes, nsa_stream_t stream);
 /* One decode step: nsa_kivi_append(new_k, new_v) then nsa_kivi_stream_decode(q),
  * with the same results and cache state.  When every unit is decoded by a
- * single CTA (units >= half the CTA slots) both run in one launch: the
+ * single CTA (more units than half the CTA slots, or any number when a unit's
+ * groups and residual all fit the kernel's stages, as at W <= 416 with
+ * residual 128) both run in one launch: the
  * decode's CTA of each unit stores the token, quantizes a completed group or
  * the sink group itself, and attends over its staged copies.  Same workspace
  * as nsa_kivi_stream_decode.  No reference counterpart (the reference has no
