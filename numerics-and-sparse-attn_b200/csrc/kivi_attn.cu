@@ -936,7 +936,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   // streaming layout: the free stages' F-tiles, one warp each: their copies are issued while
   // lane 0 of warp 0 issues batch 0 (each copy request takes hundreds of cycles to issue):
   // -0.1 to -0.2 us.  (The reference layout's tile loads need the tensor maps lane 0 prefetches.)
-  // (kLateTile1: F-tile 1 waits for the length below and covers only the rows read)
+  // (kLateTile1: F-tile 1 is issued once the length below has arrived)
   if (kRec && !kSized && lane == 0 && warp >= 1)
     for (int i = warp - 1; i < (kLateTile1 ? 1 : kFStages); i += kCWarps - 1) iss.first_f(i);
   int len = static_cast<int>(len64);
@@ -950,7 +950,7 @@ __device__ __forceinline__ void kivi_decode_cta(const CUtensorMap* tmK, const CU
   if (!kSimple && leader) iss.pump_q(meta, 0);
   if (kRec && kSized && lane == 0 && warp >= 1)
     for (int i = warp - 1; i < kFStages; i += kCWarps - 1) iss.first_f_sized(i, meta, ap.fl_s0);
-  if (kRec && !kSized && kLateTile1 && lane == 0 && warp == 2) iss.first_f_sized(1, meta, ap.fl_s0);
+  if (kRec && !kSized && kLateTile1 && lane == 0 && warp == 2) iss.first_f(1);
   sts128(smem_u32(&sm.qpad[ct >> 4][(ct & 15) * 8]), qv.x, qv.y, qv.z, qv.w);
   if (appending) {
     sm.newtok[0][ct] = new_kc;
@@ -1165,11 +1165,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 // at B=32.  Longer windows attend nearly every slot and keep the copies that
 // need no length, in their own instantiation.
 //
-// A one-layer launch copies F-tile 1 (the second 80 slots) only once the
-// unit's length is known, and only the rows it reads: F-tile 0 and batch 0
-// keep DRAM busy meanwhile (W=256 step 7.59 -> 7.43 us, DRAM bytes -1 MB).
-// The layer-batched launch keeps the blind copy (there the wait measured
-// +0.19 us per layer).
+// A one-layer launch issues the copy of F-tile 1 (the second 80 slots) only
+// once the unit's length has arrived, ~0.9 us after the grid wait: batch 0
+// and F-tile 0 of every unit then reach the SMs first, so their work is done
+// when F-tile 1 lands (W=256 step 7.59 -> 7.37 us; covering only the rows
+// read as well measured 0.03 us slower, and waiting for batch 0 to land
+// 0.2 us slower).  The layer-batched launch, whose CTAs start at staggered
+// times, issues both at once (the late copy measured +0.19 us per layer).
 template <bool kSized, bool kSimple>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) kivi_stream_decode_kernel(const KParams p) {
   kivi_decode_cta<true, false, kSized, kSimple, true>(nullptr, nullptr, p, blockIdx.x);
