@@ -185,11 +185,14 @@ def _compare_state(cache, k_hist, v_hist, L, geom):
             np.testing.assert_array_equal(got[key][:, :, rows], ref[key][:, :, rows], err_msg=f"{key} at L={L}")
 
 
-@pytest.mark.parametrize("W", [256, 128, 32, 192])
+@pytest.mark.parametrize("W", [256, 128, 32, 192, 64, 384])
 def test_stream_append_from_empty_matches_oracle(W):
     """Appends from an empty cache through the sink re-quantization (steps
     1-4), ramp-up, the first group flushes and window eviction; the state is
-    checked bit-exactly and the attention output against the oracle."""
+    checked bit-exactly and the attention output against the oracle.  B=2:
+    one CTA per unit and the append inside the decode launch at every window
+    here -- the resident-only kernel at W <= 256, residual copies covering the
+    attended rows only at W < 128, two Q-batches at W=384."""
     B, Hkv, S, R = 2, 8, 4, 128
     geom = ok.StreamGeometry(window=W, sink=S, residual=R)
     n_steps = S + W + R + 3 * 32 + 5
