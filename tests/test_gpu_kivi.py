@@ -348,14 +348,15 @@ def test_large_residual_ring_refills_residual_stages(R, W):
         np.testing.assert_array_equal(a[key], b[key], err_msg=key)
 
 
-def test_layer_batched_step_equals_per_layer_steps():
-    """decode_step_layers (3 layers in one launch) gives the same cache states,
-    bit for bit, and the same outputs up to rounding (accumulation order) as
-    KiviCache.decode_step layer by layer, over steps that include a group
-    flush."""
+@pytest.mark.parametrize("W", [256, 32])
+def test_layer_batched_step_equals_per_layer_steps(W):
+    """decode_step_layers (3 layers in one launch) gives the same cache
+    states, bit for bit, and the same outputs up to rounding (accumulation
+    order) as KiviCache.decode_step layer by layer, over steps that include a
+    group flush (W=256) or copies of the attended residual rows only (W=32)."""
     import importlib
     kivi = importlib.import_module("numerics-and-sparse-attn_b200.kivi")
-    B, Hkv, W, L, n = 32, 8, 256, 163_840, 3
+    B, Hkv, L, n = 32, 8, 163_840, 3
 
     def make():
         g = torch.Generator(device=DEV).manual_seed(123)
