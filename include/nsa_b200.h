@@ -241,6 +241,10 @@ int nsa_kivi_append(const nsa_kivi_stream_cache* cache, const void* new_k, const
                     nsa_stream_t stream);
 /* Decode q [B, 8*Hkv, D] against the streaming cache -> o. */
 size_t nsa_kivi_stream_workspace_bytes(const nsa_kivi_stream_cache* cache);
+/* Kernel launches one nsa_kivi_stream_decode_step of this cache takes on the
+ * current device: 1 (append inside the decode launch) or 2 (append, then
+ * decode); 0 for an invalid descriptor.  Computes the plan only. */
+int nsa_kivi_stream_step_launches(const nsa_kivi_stream_cache* cache);
 int nsa_kivi_stream_decode(const nsa_kivi_stream_cache* cache, const void* q, void* o, float sm_scale,
                            void* workspace, size_t workspace_bytes, nsa_stream_t stream);
 /* One decode step: nsa_kivi_append(new_k, new_v) then nsa_kivi_stream_decode(q),

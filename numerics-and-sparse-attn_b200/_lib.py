@@ -53,6 +53,7 @@ PROTOTYPES = {
     "nsa_kivi_decode": (_INT, [_P] * 16 + [_I64] * 10 + [_F, _P, _SZ, _P]),
     "nsa_kivi_append": (_INT, [_P, _P, _P, _P]),
     "nsa_kivi_stream_workspace_bytes": (_SZ, [_P]),
+    "nsa_kivi_stream_step_launches": (_INT, [_P]),
     "nsa_kivi_stream_decode": (_INT, [_P, _P, _P, _F, _P, _SZ, _P]),
     "nsa_kivi_stream_decode_step": (_INT, [_P, _P, _P, _P, _P, _F, _P, _SZ, _P]),
     "nsa_kivi_stream_decode_step_layers": (_INT, [_P, _I64, _P, _P, _P, _P, _F, _P, _SZ, _P]),

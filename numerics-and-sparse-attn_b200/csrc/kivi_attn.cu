@@ -1500,6 +1500,11 @@ int nsa_kivi_stream_decode_step(const nsa_kivi_stream_cache* cache, const void* 
   return nsa_kivi_stream_decode(cache, q, o, sm_scale, workspace, workspace_bytes, stream);
 }
 
+int nsa_kivi_stream_step_launches(const nsa_kivi_stream_cache* c) {
+  if (!c || c->batch < 0 || c->n_kv_heads <= 0 || c->residual <= 0) return 0;
+  return stream_plan(*c).ppu == 1 && fused_append_enabled() ? 1 : 2;
+}
+
 int nsa_kivi_stream_decode_step_layers(const nsa_kivi_stream_cache* caches, int64_t n_layers,
                                        const void* const* new_k, const void* const* new_v, const void* const* q,
                                        void* const* o, float sm_scale, void* workspace, size_t workspace_bytes,

@@ -354,13 +354,12 @@ class KiviCache:
         return o
 
     def step_launches(self) -> int:
-        """Kernel launches of one decode_step: 1 when every unit is decoded
-        by its own CTA (units > half the CTA slots, two per SM), else 2."""
-        if os.environ.get("NSA_FUSED_APPEND", "1").startswith("0"):
-            return 2
-        slots = 2 * torch.cuda.get_device_properties(self.device).multi_processor_count
-        units = self.batch * self.n_kv_heads
-        return 1 if units >= slots or 2 * units > slots else 2
+        """Kernel launches of one decode_step, as the library plans it on this
+        cache's device: 1 when every unit is decoded by its own CTA (more units
+        than half the CTA slots, or units whose groups and residual all fit the
+        kernel's stages), else 2."""
+        with torch.cuda.device(self.device):
+            return int(_lib.load().nsa_kivi_stream_step_launches(ctypes.byref(self._desc)))
 
     def decode_step(self, q, new_k, new_v, sm_scale=None, out=None):
         """One decode step: quantize-on-append of the new token, then attend

@@ -378,6 +378,17 @@ def test_layer_batched_step_equals_per_layer_steps(W):
             np.testing.assert_array_equal(sa[key], sb[key], err_msg=key)
 
 
+@pytest.mark.parametrize("B,W,launches", [(32, 256, 1), (2, 256, 1), (1, 416, 1), (2, 1024, 2), (32, 1024, 1)])
+def test_step_launch_plan(B, W, launches):
+    """One launch per decode step when every unit keeps its own CTA: at B=32
+    (256 units, more than half the 296 CTA slots), and at any batch when a
+    unit's groups and residual all fit the kernel's stages (W <= 416 with
+    residual 128); small batches of long windows split their units and
+    append in a launch of its own."""
+    cache = quant_kernel.KiviCache(B, 8, W, device=DEV)
+    assert cache.step_launches() == launches
+
+
 def test_no_device_error_recorded():
     import importlib
     pkg = importlib.import_module("numerics-and-sparse-attn_b200")
