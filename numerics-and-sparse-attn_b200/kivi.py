@@ -14,7 +14,6 @@ semantics are documented with ``nsa_kivi_stream_cache`` in include/nsa_b200.h.
 from __future__ import annotations
 
 import ctypes
-import os
 
 import torch
 
