@@ -3,9 +3,10 @@
 // ring layout of nsa_kivi_stream_cache.
 //
 // Work: one CTA per piece, two CTAs per SM.  A piece is one unit (batch row,
-// KV head) -- or, when there are fewer units than CTA slots, a contiguous part
-// of the unit's items, merged by the split-K combine.  With every unit resident
-// at once, all of a launch's loads are in flight from the start.  Per unit the
+// KV head) -- or, for long windows with fewer units than CTA slots, a
+// contiguous part of the unit's items, merged by the split-K combine (units
+// whose items all fit the stages keep one CTA at any batch).  With every unit
+// resident at once, all of a launch's loads are in flight from the start.  Per unit the
 // items, in issue and consumption order, are: Q-batch 0, the F-tiles, the
 // other Q-batches, where
 //   Q-batch    up to 5 quantized 32-token groups (slot 0 of batch 0 is the
@@ -23,8 +24,10 @@
 // and its dequantization overlaps the residual's transfer.  Every copy request
 // costs a fixed issue time (about 40 ns on B200) whatever its size, so loads
 // are few and large, and those that do not depend on the unit's length (query,
-// batch 0, residual) are issued before that length is read.  Q-batches after
-// the first that hold no attended token are skipped by every warp alike.
+// batch 0, residual) are issued before that length is read -- except, in a
+// one-layer streaming launch, the second F-tile, which waits for the length so
+// that batch 0 and the first F-tile of every unit arrive first.  Q-batches
+// after the first that hold no attended token are skipped by every warp alike.
 //
 // Warps 0-3 consume, each claiming the next job of the staged item (a
 // quantized group, or 32 rows of an F-tile) from a shared-memory counter as
