@@ -87,7 +87,7 @@ def algorithmic_bytes(workload: str, batch: int) -> int:
 # dominant kernel at B=32, from the committed ncu captures of this exact workload.
 NCU_TRAFFIC = {
     "kivi": (25_627_136, "profiles/kivi_stream_step_kernel_kivi_W256_L163840_B32.md"),
-    "sparse": (34_633_984, "profiles/window_decode_kernel_sparse_W256_L163840_B32.md"),
+    "sparse": (34_629_632, "profiles/window_decode_kernel_sparse_W256_L163840_B32.md"),
     "dense": (1_078_491_176, "profiles/fp16_decode_kernel_dense_L8192_B32.md"),
 }
 
