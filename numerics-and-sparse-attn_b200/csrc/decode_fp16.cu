@@ -200,7 +200,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const Params p) {
   extern __shared__ uint8_t smem_raw[];
   grid_launch_dependents();
-  grid_dependency_wait();  // the cache and q may come from the previous kernel of the stream
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -216,6 +215,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
   }
   __syncthreads();
+  // the cache and q may come from the previous kernel of the stream: global
+  // memory is read only after this wait (the barriers are initialised first:
+  // -0.12 us per W=1024 launch at B=32)
+  grid_dependency_wait();
 
   // CTA-local tile k (over all pieces in order) lives in stage k % kStages,
   // phase (k / kStages) & 1, and is consumed by group k % kGroups.
