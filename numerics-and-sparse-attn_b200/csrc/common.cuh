@@ -130,6 +130,13 @@ __device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int c0, 
                "r"(c0), "r"(c1), "r"(c2), "r"(c3)
                : "memory");
 }
+// Prefetch a 3-D tensor-map box into L2 (coordinates innermost first).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
 // Prefetch [src, src + bytes) into L2 (16-byte aligned, a multiple of 16
 // bytes): no shared memory, no completion; a later load of the range then
 // waits on L2 instead of DRAM.
